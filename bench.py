@@ -1,0 +1,475 @@
+"""Benchmark of the B200 int4 (Q4NX / w4) decode path.
+
+Workload (one step = one token): the Llama-3-8B-shaped decode linear set at
+batch 1 -- 32 layers x {QKV 4096->6144, O 4096->4096, gate 4096->14336,
+up 4096->14336, down 14336->4096} -- with independent seeded random int4
+weights per layer (group 32, bf16 scales |N(0,0.02)|/7.5, zero point 8) and
+bf16 N(0,1) activations; each projection reads a fixed activation, as the
+reference's projection-stream benchmark does (crates/xnpu-cli/src/main.rs:
+2487-2499, :3288).  3.93 GB of weights per step, far above the 126 MB L2, so
+no flush is needed between steps.
+
+On N GPUs (torchrun, one process per GPU) the FFN gate/up projections are
+column-sharded N ways and their outputs all-gathered over NCCL each layer;
+QKV, O and down are replicated.  The step is the same token, so scaling is
+"strong".  The line also reports the lm_head 4096->128256 (f32 logits)
+sharded the same way.
+
+Metric: tokens/s (higher is better); GB/s of algorithmic bytes (packed codes
++ scales + x + y) and its fraction of the measured HBM peak are in
+``roofline``.  ``--impl reference`` times the reference's CPU path (the C
+restatement in oracle/, all host threads) on a bounded row sample.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+LAYERS = 32
+SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate", 14336, 4096), ("up", 14336, 4096),
+          ("down", 4096, 14336)]
+LMHEAD = (128256, 4096)
+
+
+def algo_bytes(n, k, m=1, out_bytes=2):
+    return n * k // 2 + n * (k // 32) * 2 + m * k * 2 + m * n * out_bytes
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"xq4_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[3:7]))
+                except ValueError:
+                    pass
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_baseline(steps=1, budget_s=12.0):
+    """The reference's CPU path (oracle restatement of main.rs:2287-2296 over
+    the L1 layout, rows split over all host threads) on a row sample of one
+    layer's five projections; scaled to tokens/s of the 32-layer set."""
+    from oracle import oracle as O
+    from xnpu_b200 import synth
+    threads = os.cpu_count() or 1
+    frac = 1.0 / 16  # rows sampled per projection
+    samples = []
+    for name, n, k in SHAPES:
+        rows = max(128, int(n * frac) // 128 * 128)
+        q = synth.unpack_codes_signed(synth.synth_codes(rows, k, 7))
+        s = synth.synth_scales(rows, k, 7)
+        tsi = 4 if name == "down" else 16
+        pack = O.l1_pack(q, s, tsi=tsi)
+        x = synth.synth_x(1, k, 7)
+        samples.append((n, k, rows, tsi, pack, x))
+    t_layer = []
+    t_end = time.time() + budget_s
+    for _ in range(max(1, steps)):
+        t = 0.0
+        for n, k, rows, tsi, pack, x in samples:
+            t0 = time.perf_counter()
+            O.gemv_l1(pack, rows, k, tsi, x, nthreads=threads)
+            t += (time.perf_counter() - t0) * (n / rows)
+        t_layer.append(t)
+        if time.time() > t_end:
+            break
+    tok_s = 1.0 / (np.median(t_layer) * LAYERS)
+    return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"1/16 of the rows of each of the 5 projections of one layer (L1 layout, sequential "
+                      f"f32 per row), {len(t_layer)} timed pass(es), scaled to 32 layers",
+            "gbs": sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS * tok_s / 1e9}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O  # noqa: F401  (builds the oracle if needed)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(steps=1, budget_s=30.0)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = float(np.median(vals))
+    line = {"metric": "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)", "value": v,
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, bf16 x, f32 accumulate", "data": "synthetic (seeded)",
+            "impl": "reference",
+            "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
+                                   "gate/up 4096x14336, down 14336x4096), M=1", "group": 32},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
+                             "sample": r["sample"]},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def make_weights(dev, rank, world, seed_base=1):
+    """All 32 layers' weights; gate/up rows sharded over ranks."""
+    from concurrent.futures import ThreadPoolExecutor
+    from xnpu_b200 import hal, synth
+
+    def one(li, si):
+        name, n, k = SHAPES[si]
+        seed = seed_base + 1000 * li + si
+        codes = synth.synth_codes(n, k, seed)
+        scales = synth.synth_scales(n, k, seed)
+        src = synth.planes_bytes(codes, scales)
+        r0, r1 = 0, 0
+        if world > 1 and name in ("gate", "up"):
+            r0, r1 = rank * n // world, (rank + 1) * n // world
+        return hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=r0, row_end=r1), src
+
+    weights = []
+    with ThreadPoolExecutor(max_workers=4) as ex:
+        for li in range(LAYERS):
+            futs = [ex.submit(one, li, si) for si in range(len(SHAPES))]
+            layer = {}
+            for si, f in enumerate(futs):
+                desc, src = f.result()
+                layer[SHAPES[si][0]] = hal.Weight.import_(dev, src, desc)
+                del src
+            weights.append(layer)
+    return weights
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="xq4", choices=["xq4", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from xnpu_b200 import hal, synth, lib
+    from xnpu_b200._lib import check
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = hal.Device.open(local)
+    meta = dev.metadata()
+    L = lib()
+
+    weights = make_weights(dev, rank, world)
+    comm = None
+    if world > 1:
+        import ctypes
+        uid = (ctypes.c_char * 128)()
+        if rank == 0:
+            check(L.xq4_comm_unique_id(ctypes.addressof(uid)))
+        t = torch.frombuffer(bytearray(bytes(uid)), dtype=torch.uint8).cuda()
+        dist.broadcast(t, 0)
+        uid = (ctypes.c_char * 128).from_buffer_copy(t.cpu().numpy().tobytes())
+        h = ctypes.c_void_p()
+        check(L.xq4_comm_init(dev.handle, rank, world, ctypes.addressof(uid), ctypes.byref(h)))
+        comm = h
+
+    # activations / outputs (fixed per shape, as the reference's stream benchmark)
+    xs = {k: torch.from_numpy(synth.synth_x(1, k, 11 + k).view(np.int16)).cuda().view(torch.bfloat16)
+          for k in (4096, 14336)}
+    ys = {name: torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for name, n, _ in SHAPES}
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def step(st):
+        launches = 0
+        for layer in weights:
+            for name, n, k in SHAPES:
+                w = layer[name]
+                if comm is not None and name in ("gate", "up"):
+                    check(L.xq4_linear_sharded(comm, w.handle, xs[k].data_ptr(), ys[name].data_ptr(), None, 1, 0, st))
+                else:
+                    check(L.xq4_linear_raw(w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
+                launches += 1
+        return launches
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(sp)
+    barrier()
+
+    # device-timed steps (inputs resident in HBM)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                launches += step(sp)
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = clk.summary()
+
+    # per-launch kernel durations for the roofline (events around each launch)
+    per = {name: [] for name, _, _ in SHAPES}
+    evs = []
+    with torch.cuda.stream(stream):
+        for layer in weights[:8]:
+            for name, n, k in SHAPES:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                if comm is not None and name in ("gate", "up"):
+                    check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
+                else:
+                    check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
+                b.record(stream)
+                evs.append((name, a, b))
+    torch.cuda.synchronize()
+    for name, a, b in evs:
+        per[name].append(a.elapsed_time(b))
+    tot_bytes = 0
+    tot_ms = 0.0
+    for name, n, k in SHAPES:
+        ns = n // world if (world > 1 and name in ("gate", "up")) else n
+        tot_bytes += algo_bytes(ns, k) * len(per[name])
+        tot_ms += sum(per[name])
+    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # end-to-end through the C ABI with host buffers (pinned), copies inside
+    e2e = e2e_run(dev, weights, comm, world, args)
+
+    # lm_head (sharded the same way), f32 logits
+    lm = lmhead_run(dev, rank, world, comm, L, stream)
+
+    step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
+    if rank == 0:
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
+        line = {
+            "metric": "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)",
+            "value": 1e3 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights (u4 codes, bf16 scales), bf16 x, f32 accumulate",
+            "data": "synthetic (seeded PCG64; random-init 8B-shaped weights)",
+            "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
+                                   "gate/up 4096x14336, down 14336x4096), M=1",
+                       "group": 32, "layers": LAYERS, "batch": 1,
+                       "parallelism": "single GPU" if world == 1 else f"gate/up column-sharded x{world} + NCCL all-gather; qkv/o/down replicated",
+                       "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
+            "gbs": step_bytes * (1e3 / ms) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "kernel": "gemv_kernel<1> (decode GEMV, m=1)",
+                         "traffic": None,
+                         "per_shape_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()}},
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "lm_head": lm,
+            "device": meta["name"],
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        check(L.xq4_comm_destroy(comm))
+    for layer in weights:
+        for w in layer.values():
+            w.destroy()
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_run(dev, weights, comm, world, args):
+    """Same step through the public C ABI with host buffers: one pinned H2D of
+    the step's activations, 160 xq4_linear submits on the device queue, one
+    D2H of every output, xq4_wait -- timed on the host clock."""
+    import ctypes
+    import torch
+    from xnpu_b200 import hal, lib, synth
+    from xnpu_b200._lib import check
+    L = lib()
+    # per step inputs: one x per distinct K (the reference's benchmark feeds a
+    # fixed activation per shape); outputs: every projection of every layer
+    k_off = {4096: 0, 14336: 4096 * 2}
+    x_bytes = (4096 + 14336) * 2
+    y_sizes = [(li, name, n) for li in range(LAYERS) for name, n, _ in SHAPES]
+    y_off, off = {}, 0
+    for li, name, n in y_sizes:
+        y_off[(li, name)] = off
+        off += ((n * 2 + 255) // 256) * 256
+    y_bytes = off
+    xb = hal.BufferObject.new(dev, x_bytes)
+    yb = hal.BufferObject.new(dev, y_bytes)
+    hx = torch.empty(x_bytes, dtype=torch.uint8).pin_memory()
+    hy = torch.empty(y_bytes, dtype=torch.uint8).pin_memory()
+    hx.numpy()[:] = synth.synth_x(1, x_bytes // 2, 5).reshape(-1).view(np.uint8)
+    seq = ctypes.c_uint64()
+
+    def one():
+        check(L.xq4_buffer_upload(xb.handle, hx.data_ptr(), 0, x_bytes))
+        for li, layer in enumerate(weights):
+            for name, n, k in SHAPES:
+                if comm is not None and name in ("gate", "up"):
+                    xp = xb.device_ptr() + k_off[k]
+                    yp = yb.device_ptr() + y_off[(li, name)]
+                    check(L.xq4_linear_sharded(comm, layer[name].handle, xp, yp, None, 1, 0,
+                                               dev.stream_handle()))
+                else:
+                    check(L.xq4_linear(dev.handle, layer[name].handle, xb.handle, k_off[k], yb.handle,
+                                       y_off[(li, name)], 1, 0, ctypes.byref(seq)))
+        check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
+        check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
+
+    import torch.distributed as dist
+    for _ in range(max(1, args.warmup)):
+        one()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    dt = (time.perf_counter() - t0) / args.steps
+    if world > 1:
+        t = torch.tensor([dt], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+    xb.destroy()
+    yb.destroy()
+    return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
+            "ms_per_step": dt * 1e3, "path": "xq4_buffer_upload -> 160 x xq4_linear -> xq4_wait -> "
+                                             "xq4_buffer_download (pinned host buffers)"}
+
+
+def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
+    """lm_head 4096 -> 128256, f32 logits, rows sharded over ranks +
+    all-gather; 8 rotating weight copies (>2x L2 at every N)."""
+    import torch
+    import torch.distributed as dist
+    from xnpu_b200 import hal, synth
+    from xnpu_b200._lib import check
+    n, k = LMHEAD
+    r0, r1 = rank * n // world, (rank + 1) * n // world
+    copies = 8 if world == 1 else max(8, 2 * world)
+    codes = synth.synth_codes(n, k, 424242)
+    scales = synth.synth_scales(n, k, 424242)
+    src = synth.planes_bytes(codes, scales)
+    ws = [hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=r0, row_end=r1))
+          for _ in range(copies)]
+    del src
+    x = torch.from_numpy(synth.synth_x(1, k, 9).view(np.int16)).cuda().view(torch.bfloat16)
+    y = torch.empty((1, n), dtype=torch.float32, device="cuda")
+    sp = stream.cuda_stream
+
+    def go(i):
+        if comm is not None:
+            check(L.xq4_linear_sharded(comm, ws[i % copies].handle, x.data_ptr(), y.data_ptr(), None, 1, 1, sp))
+        else:
+            check(L.xq4_linear_raw(ws[i % copies].handle, x.data_ptr(), y.data_ptr(), 1, 1, sp))
+
+    with torch.cuda.stream(stream):
+        for i in range(5):
+            go(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    with torch.cuda.stream(stream):
+        for i in range(reps):
+            go(i)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    for w in ws:
+        w.destroy()
+    shard_bytes = algo_bytes(r1 - r0, k, out_bytes=4)
+    return {"us": ms * 1e3, "shard_rows": r1 - r0, "gbs_per_gpu": shard_bytes / (ms * 1e-3) / 1e9,
+            "logits_allgather_bytes": n * 4 if world > 1 else 0}
+
+
+if __name__ == "__main__":
+    main()

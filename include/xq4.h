@@ -1,0 +1,205 @@
+/*
+ * xq4.h -- C ABI of the B200 (sm_100a) backend for xnpu's int4 ("w4" / Q4NX)
+ * weight-matrix path.
+ *
+ * The reference (nzinfo/xnpu) drives this path through its HAL crate
+ * (crates/xnpu-hal): open a device, create buffer objects, upload weights and
+ * activations, submit one op packet whose arguments are [W, x, C], and wait on
+ * a timeline point with a deadline.  Each entry point below replaces one piece
+ * of that surface and names the reference item it stands in for.  All calls
+ * return an int status (XQ4_OK on success); the message of the last failure
+ * on the calling thread is available from xq4_last_error_string().
+ *
+ * Ownership: every handle is created by one call and released by exactly one
+ * destroy/close call (the reference's RAII: Device owns fd + heap,
+ * crates/xnpu-hal/src/accel.rs:107-116; BufferObject closes its handle on drop,
+ * crates/xnpu-hal/src/bo.rs:160-181).  Handles are not thread-safe; use one
+ * device handle (one in-order queue) per thread, as the reference does
+ * (one in-order queue per context, crates/xnpu-cli/src/main.rs:1637-1641).
+ *
+ * Numerics: int4 codes q in [-8, 7] with one bf16 scale per 32 consecutive K
+ * values of a row; dequantized weight w = RNE_bf16(f32(q) * f32(scale))
+ * (crates/xnpu-cli/src/main.rs:3097-3125); y = sum_k w*x accumulated in f32,
+ * rounded once to the output type (crates/xnpu-cli/src/main.rs:2287-2296).
+ */
+#ifndef XQ4_H
+#define XQ4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+/* The reference reports std::io::Result errno (crates/xnpu-hal/src/ioctl.rs:59-66)
+ * and a timeline-wait timeout as an error (crates/xnpu-hal/src/ert.rs:214-261). */
+#define XQ4_OK 0
+#define XQ4_EINVAL 1     /* bad argument, size, layout or alignment */
+#define XQ4_ENOMEM 2     /* device or host allocation failed */
+#define XQ4_ECUDA 3      /* CUDA runtime/driver error (message has the detail) */
+#define XQ4_ETIMEDOUT 4  /* xq4_wait deadline passed before completion */
+#define XQ4_ENCCL 5      /* NCCL error in the sharded path */
+#define XQ4_ENOTSUP 6    /* valid request this build does not implement */
+#define XQ4_ENODEV 7     /* no usable sm_100 device at that ordinal */
+
+/* ---------------------------------------------------------------- layouts */
+/* Source layouts accepted by xq4_weight_import. */
+#define XQ4_LAYOUT_L1 1     /* w4gemv2 tile layout written by tools/w4_import.py
+                               (crates/xnpu-cli/src/main.rs:2186-2252) */
+#define XQ4_LAYOUT_L2 2     /* w4gemvu v4/v5 16x2048 block layout, the "Q4NX" pack
+                               (crates/xnpu-cli/src/main.rs:2912-2949, :3097-3125) */
+#define XQ4_LAYOUT_PLANES 3 /* row-major planes: codes [n][k/2] bytes (low nibble =
+                               even k) then scales [n][k/group] at scale_offset */
+
+#define XQ4_CODE_S4 0       /* nibble = two's-complement q (the reference's ABI) */
+#define XQ4_CODE_U4_ZP8 1   /* nibble = q + 8, code in [0, 15], zero point 8 */
+
+#define XQ4_SCALE_BF16 0
+#define XQ4_SCALE_FP16 1    /* must be exactly representable in bf16 */
+
+#define XQ4_OUT_BF16 0      /* output rounded RNE to bf16 */
+#define XQ4_OUT_F32 1       /* output kept in f32 (logits) */
+
+typedef struct xq4_layout_desc {
+    int layout;        /* XQ4_LAYOUT_* */
+    int n;             /* rows (output features) of the FULL matrix in src */
+    int k;             /* reduction length; multiple of 32 */
+    int group;         /* must be 32 */
+    int tsi;           /* L1 only: rows per tile (16 or 4 in the reference) */
+    int cols;          /* L1 only: column count (8 in the reference) */
+    int code_format;   /* PLANES only: XQ4_CODE_* */
+    int scale_dtype;   /* PLANES only: XQ4_SCALE_* */
+    size_t scale_offset; /* PLANES only: byte offset of the scale plane in src */
+    int row_begin;     /* import rows [row_begin, row_end) of src; both 0 = all */
+    int row_end;
+} xq4_layout_desc;
+
+typedef struct xq4_device xq4_device;
+typedef struct xq4_buffer xq4_buffer;
+typedef struct xq4_weight xq4_weight;
+typedef struct xq4_comm xq4_comm;
+
+typedef struct xq4_device_info {
+    int ordinal;
+    int sm_count;
+    int cc_major, cc_minor;
+    size_t hbm_bytes;
+    size_t l2_bytes;
+    char name[96];
+} xq4_device_info;
+
+/* ---------------------------------------------------------------- errors */
+/* Message of the last failing call on this thread ("" if none). */
+const char *xq4_last_error_string(void);
+/* Library version string. */
+const char *xq4_version(void);
+
+/* ---------------------------------------------------------------- device */
+/* Replaces Device::open_default / Device::open (crates/xnpu-hal/src/accel.rs:122,
+ * :144) plus HwContext::create + configure_cus (crates/xnpu-hal/src/hwctx.rs:28,
+ * :95): binds CUDA device `ordinal`, creates its in-order stream and timeline. */
+int xq4_device_open(int ordinal, xq4_device **out);
+/* Replaces Device / HwContext drop (accel.rs:107-116, hwctx.rs:154-193). */
+int xq4_device_close(xq4_device *dev);
+/* Replaces Device::aie_metadata (crates/xnpu-hal/src/accel.rs:248). */
+int xq4_device_query(const xq4_device *dev, xq4_device_info *info);
+/* The device's in-order stream (a cudaStream_t), for callers that interleave
+ * their own work; the reference's queue is per context (hwctx.rs:12). */
+void *xq4_device_stream(xq4_device *dev);
+
+/* ---------------------------------------------------------------- buffers */
+/* Replaces BufferObject::new(dev, BoType, size) (crates/xnpu-hal/src/bo.rs:42).
+ * Device memory, 256-byte aligned. */
+int xq4_buffer_create(xq4_device *dev, size_t bytes, xq4_buffer **out);
+/* Replaces write through Mapping + sync(ToDevice, off, len)
+ * (crates/xnpu-hal/src/bo.rs:134, accel.rs:186).  Stream-ordered on the
+ * device's queue; returns after the host copy is consumed. */
+int xq4_buffer_upload(xq4_buffer *buf, const void *host, size_t offset, size_t len);
+/* Replaces sync(FromDevice) + read through Mapping (bo.rs:134, accel.rs:209).
+ * Waits for all queued work on the device first (in-order queue). */
+int xq4_buffer_download(xq4_buffer *buf, void *host, size_t offset, size_t len);
+/* Replaces BufferObject drop (crates/xnpu-hal/src/bo.rs:160-181). */
+int xq4_buffer_destroy(xq4_buffer *buf);
+/* Device address of the buffer; replaces BufferObject::xdna_addr (bo.rs:130). */
+void *xq4_buffer_device_ptr(const xq4_buffer *buf);
+size_t xq4_buffer_size(const xq4_buffer *buf);
+
+/* ---------------------------------------------------------------- weights */
+/* Offline import: repack src (host bytes, in `desc->layout`) into the GPU
+ * layout and upload it.  Replaces the weight-buffer upload of the reference
+ * (chain_tensor, crates/xnpu-cli/src/main.rs:1589-1603, over files written by
+ * tools/w4_import.py:116-120) and its size check (main.rs:2597).  The
+ * dequantized values are bit-identical to the source layout's.  The row range
+ * selects a column shard of the matrix (the reference splits rows across its
+ * 8 AIE columns, main.rs:2186-2191). */
+int xq4_weight_import(xq4_device *dev, const void *src, size_t src_len,
+                      const xq4_layout_desc *desc, xq4_weight **out);
+int xq4_weight_destroy(xq4_weight *w);
+/* Rows, reduction length and bytes resident in HBM for the weight. */
+int xq4_weight_shape(const xq4_weight *w, int *n, int *k, size_t *device_bytes);
+/* Repack only (no device): size of the GPU-layout image for n x k. */
+size_t xq4_gpu_layout_bytes(int n, int k);
+/* Repack only (no device): write the GPU-layout image of src rows
+ * [row_begin,row_end) into dst (xq4_gpu_layout_bytes bytes). */
+int xq4_repack_host(const void *src, size_t src_len, const xq4_layout_desc *desc,
+                    void *dst, size_t dst_len);
+
+/* Dequantize the whole weight to bf16, row-major [n][k], into device memory
+ * at out_dev (n*k*2 bytes), on `stream` (NULL = the weight's device stream).
+ * Restates w4u_row_bf16 (crates/xnpu-cli/src/main.rs:3102-3125) for every row. */
+int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream);
+
+/* ---------------------------------------------------------------- the op */
+/* y[m][n] = x[m][k] . dequant(W)^T.  Replaces building and submitting one
+ * w4 GEMV op packet with args [W, x, C] (StartNpuCmd::new/arg64/submit,
+ * crates/xnpu-hal/src/ert.rs:77-212; chain_op, crates/xnpu-cli/src/main.rs:
+ * 1611-1635) and returns its timeline point in *seq (may be NULL).
+ * x: bf16 [m][k] at x_off bytes into x_buf; y: [m][n] of out_dtype at y_off.
+ * m <= 15 runs the decode GEMV kernel, m >= 16 the tensor-core GEMM. */
+int xq4_linear(xq4_device *dev, const xq4_weight *w,
+               const xq4_buffer *x_buf, size_t x_off,
+               xq4_buffer *y_buf, size_t y_off,
+               int m, int out_dtype, uint64_t *seq);
+
+/* Same op on raw device pointers and a caller stream (a cudaStream_t; NULL =
+ * the weight's device stream).  x and y must be 16-byte aligned. */
+int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev,
+                   int m, int out_dtype, void *stream);
+
+/* Replaces syncobj_timeline_wait(dev, syncobj, seq, timeout_ns)
+ * (crates/xnpu-hal/src/ert.rs:218) and the completed-state check
+ * (ert.rs:147-151): XQ4_OK when the op at `seq` and everything queued before
+ * it has completed, XQ4_ETIMEDOUT if timeout_ns elapsed first (the work stays
+ * queued and a later wait may succeed), XQ4_ECUDA if the device reported an
+ * error. */
+int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns);
+/* Timeline point of the newest submitted op. */
+uint64_t xq4_last_seq(const xq4_device *dev);
+
+/* ---------------------------------------------------------------- shards */
+/* Column (N) sharding of large-N projections over P GPUs with an NCCL
+ * all-gather of the outputs.  The reference is single-device; its nearest
+ * counterpart is the row split over AIE columns with a host gather of the
+ * per-column C sections (w4u_read_c, crates/xnpu-cli/src/main.rs:3066-3091). */
+#define XQ4_UNIQUE_ID_BYTES 128
+int xq4_comm_unique_id(void *id_out /* XQ4_UNIQUE_ID_BYTES */);
+int xq4_comm_init(xq4_device *dev, int rank, int nranks, const void *unique_id,
+                  xq4_comm **out);
+int xq4_comm_destroy(xq4_comm *comm);
+/* y_full[m][n_total] = x . W^T where this rank holds rows
+ * [rank*n_shard, (rank+1)*n_shard) of W (n_shard = its weight's n, equal on
+ * every rank).  Computes the local slice, all-gathers the slices over NCCL and
+ * leaves the full output on every rank.  y_full needs m*n_shard*nranks
+ * elements of out_dtype; ws (scratch of the same size) may be NULL when
+ * m == 1. */
+int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w_shard,
+                       const void *x_dev, void *y_full_dev, void *ws_dev,
+                       int m, int out_dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XQ4_H */

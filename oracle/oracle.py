@@ -1,0 +1,220 @@
+"""ctypes wrapper of the C oracle (q4nx_oracle.c) -- TEST INFRASTRUCTURE ONLY.
+
+Used by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg as the
+checker / the timed CPU restatement of the reference.  The shipped library
+never imports this module.
+"""
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "libq4nx_oracle.so"
+_L = None
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i8p = ctypes.POINTER(ctypes.c_int8)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_I = ctypes.c_int
+_SZ = ctypes.c_size_t
+
+_SIGS = {
+    "q4o_f32_to_bf16": (ctypes.c_uint16, [ctypes.c_float]),
+    "q4o_bf16_to_f32": (ctypes.c_float, [ctypes.c_uint16]),
+    "q4o_dequant_one": (ctypes.c_uint16, [_I, ctypes.c_uint16]),
+    "q4o_l1_size": (_SZ, [_I, _I, _I, _I, _I]),
+    "q4o_l1_pack": (_I, [_i8p, _u16p, _I, _I, _I, _I, _I, _u8p]),
+    "q4o_l1_unpack": (_I, [_u8p, _I, _I, _I, _I, _I, _i8p, _u16p]),
+    "q4o_l1_dequant_rows": (_I, [_u8p, _I, _I, _I, _I, _I, _I, _I, _u16p]),
+    "q4o_l2_size": (_SZ, [_I, _I]),
+    "q4o_l2_pack": (_I, [_i8p, _u16p, _I, _I, _u8p]),
+    "q4o_l2_dequant_rows": (_I, [_u8p, _I, _I, _I, _I, _u16p]),
+    "q4o_l2_row_ref": (_I, [_u8p, _I, _I, _I, _u16p]),
+    "q4o_gemv_bf16": (_I, [_u16p, _u16p, _I, _I, _I, _f32p, _I]),
+    "q4o_gemv_l1": (_I, [_u8p, _I, _I, _I, _I, _I, _u16p, _I, _f32p, _I]),
+    "q4o_gemv_l2": (_I, [_u8p, _I, _I, _u16p, _I, _f32p, _I]),
+    "q4o_round_bf16": (None, [_f32p, _SZ, _u16p]),
+    "q4o_kat_fill": (None, [_I, _I, _I, _i8p, _u16p, _u16p]),
+    "q4o_kat_ref": (None, [_I, _I, _I, _u16p]),
+    "q4o_quantize_x": (_I, [_u16p, _I, _i8p, _u16p]),
+    "q4o_sum_chunk_partials": (None, [_u16p, _I, _I, _u16p]),
+}
+
+
+def build():
+    """Compile the oracle (make in oracle/)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB
+
+
+def lib():
+    global _L
+    if _L is None:
+        if not LIB.exists() or LIB.stat().st_mtime < (HERE / "q4nx_oracle.c").stat().st_mtime:
+            build()
+        L = ctypes.CDLL(str(LIB))
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _L = L
+    return _L
+
+
+def _p(a, t):
+    return a.ctypes.data_as(t)
+
+
+def _ok(rc, what):
+    if rc != 0:
+        raise ValueError(f"oracle {what} rejected its arguments (rc={rc})")
+
+
+def f32_to_bf16(x):
+    return lib().q4o_f32_to_bf16(x)
+
+
+def bf16_to_f32(b):
+    return lib().q4o_bf16_to_f32(b)
+
+
+def dequant_one(q, scale_bits):
+    return lib().q4o_dequant_one(q, scale_bits)
+
+
+def l1_size(n, k, tsi, cols=8, group=32):
+    return lib().q4o_l1_size(n, k, group, tsi, cols)
+
+
+def l1_pack(q, s, tsi, cols=8, group=32):
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(s, dtype=np.uint16)
+    n, k = q.shape
+    out = np.empty(l1_size(n, k, tsi, cols, group), dtype=np.uint8)
+    _ok(lib().q4o_l1_pack(_p(q, _i8p), _p(s, _u16p), n, k, group, tsi, cols, _p(out, _u8p)), "l1_pack")
+    return out
+
+
+def l1_unpack(pack, n, k, tsi, cols=8, group=32):
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    q = np.empty((n, k), dtype=np.int8)
+    s = np.empty((n, k // group), dtype=np.uint16)
+    _ok(lib().q4o_l1_unpack(_p(pack, _u8p), n, k, group, tsi, cols, _p(q, _i8p), _p(s, _u16p)), "l1_unpack")
+    return q, s
+
+
+def l1_dequant(pack, n, k, tsi, cols=8, group=32, r0=0, r1=None):
+    r1 = n if r1 is None else r1
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    w = np.empty((r1 - r0, k), dtype=np.uint16)
+    _ok(lib().q4o_l1_dequant_rows(_p(pack, _u8p), n, k, group, tsi, cols, r0, r1, _p(w, _u16p)), "l1_dequant")
+    return w
+
+
+def l2_size(n, k):
+    return lib().q4o_l2_size(n, k)
+
+
+def l2_pack(q, s):
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(s, dtype=np.uint16)
+    n, k = q.shape
+    out = np.empty(l2_size(n, k), dtype=np.uint8)
+    _ok(lib().q4o_l2_pack(_p(q, _i8p), _p(s, _u16p), n, k, _p(out, _u8p)), "l2_pack")
+    return out
+
+
+def l2_dequant(pack, n, k, r0=0, r1=None):
+    r1 = n if r1 is None else r1
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    w = np.empty((r1 - r0, k), dtype=np.uint16)
+    _ok(lib().q4o_l2_dequant_rows(_p(pack, _u8p), n, k, r0, r1, _p(w, _u16p)), "l2_dequant")
+    return w
+
+
+def l2_row_ref(pack, n, k, row):
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    out = np.empty(k, dtype=np.uint16)
+    _ok(lib().q4o_l2_row_ref(_p(pack, _u8p), n, k, row, _p(out, _u16p)), "l2_row_ref")
+    return out
+
+
+def dequant_planes(q, s, group=32):
+    """w = RNE_bf16(q * s) for int8 q [n,k] and bf16 scale bits [n,k/group]
+    (the reference rule, main.rs:3121), vectorised; identical to the C path."""
+    qf = np.asarray(q, dtype=np.float32)
+    sf = (np.asarray(s, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+    prod = qf * np.repeat(sf, group, axis=1)
+    b = prod.view(np.uint32)
+    return ((b + np.uint32(0x7FFF) + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def gemv_bf16(w, x, nthreads=8):
+    """f32 y[m][n] (before the final RNE) from bf16 bits w [n,k] and x [m,k]."""
+    w = np.ascontiguousarray(w, dtype=np.uint16)
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    n, k = w.shape
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _ok(lib().q4o_gemv_bf16(_p(w, _u16p), _p(x, _u16p), m, n, k, _p(y, _f32p), nthreads), "gemv_bf16")
+    return y
+
+
+def gemv_l1(pack, n, k, tsi, x, cols=8, group=32, nthreads=8):
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _ok(lib().q4o_gemv_l1(_p(pack, _u8p), n, k, group, tsi, cols, _p(x, _u16p), m, _p(y, _f32p), nthreads),
+        "gemv_l1")
+    return y
+
+
+def gemv_l2(pack, n, k, x, nthreads=8):
+    pack = np.ascontiguousarray(pack, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _ok(lib().q4o_gemv_l2(_p(pack, _u8p), n, k, _p(x, _u16p), m, _p(y, _f32p), nthreads), "gemv_l2")
+    return y
+
+
+def round_bf16(y):
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty(y.shape, dtype=np.uint16)
+    lib().q4o_round_bf16(_p(y, _f32p), y.size, _p(out, _u16p))
+    return out
+
+
+def kat_fill(n, k, group=32):
+    q = np.empty((n, k), dtype=np.int8)
+    s = np.empty((n, k // group), dtype=np.uint16)
+    x = np.empty(k, dtype=np.uint16)
+    lib().q4o_kat_fill(n, k, group, _p(q, _i8p), _p(s, _u16p), _p(x, _u16p))
+    return q, s, x
+
+
+def kat_ref(n, k, group=32):
+    c = np.empty(n, dtype=np.uint16)
+    lib().q4o_kat_ref(n, k, group, _p(c, _u16p))
+    return c
+
+
+def quantize_x(x):
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    k = x.size
+    q = np.empty(k, dtype=np.int8)
+    d = np.empty(k // 32, dtype=np.uint16)
+    _ok(lib().q4o_quantize_x(_p(x, _u16p), k, _p(q, _i8p), _p(d, _u16p)), "quantize_x")
+    return q, d
+
+
+def sum_chunk_partials(parts):
+    parts = np.ascontiguousarray(parts, dtype=np.uint16)
+    c, n = parts.shape
+    out = np.empty(n, dtype=np.uint16)
+    lib().q4o_sum_chunk_partials(_p(parts, _u16p), c, n, _p(out, _u16p))
+    return out

@@ -1,0 +1,30 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return ROOT / "tests" / "golden"
+
+
+@pytest.fixture(scope="session")
+def dev():
+    """Device 0 through the C ABI (GPU tests only; no skip: a GPU run without
+    the library or the device must fail loudly)."""
+    import torch
+    from xnpu_b200 import hal
+    torch.cuda.init()
+    d = hal.Device.open_default()
+    yield d
+    d.close()

@@ -1,0 +1,56 @@
+"""The C ABI library loads on a CPU-only host and exports every entry point
+declared in include/xq4.h (no compute calls here)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from xnpu_b200 import _lib, hal
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "xq4.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(xq4_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("xq4_device_open", "xq4_buffer_create", "xq4_weight_import", "xq4_linear", "xq4_wait",
+                 "xq4_linear_sharded", "xq4_dequant", "xq4_last_error_string"):
+        assert must in names
+
+
+def test_every_declared_symbol_is_exported():
+    L = ctypes.CDLL(str(_lib.LIB_PATH))
+    missing = [n for n in declared_functions() if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_the_header():
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+    _lib.lib()  # binds every signature
+
+
+def test_version_and_error_string():
+    L = _lib.lib()
+    assert b"sm_100a" in L.xq4_version()
+    assert L.xq4_last_error_string() is not None
+
+
+def test_layout_bytes():
+    assert hal.gpu_layout_bytes(4096, 4096) == 256 * 64 * 576
+    assert hal.gpu_layout_bytes(17, 96) == 2 * 2 * 576
+    assert hal.gpu_layout_bytes(16, 33) == 0  # k must be a multiple of 32
+
+
+def test_device_open_without_gpu_fails_cleanly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    with pytest.raises(_lib.Xq4Error) as ei:
+        hal.Device.open_default()
+    assert ei.value.status == _lib.XQ4_ENODEV

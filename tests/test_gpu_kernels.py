@@ -1,0 +1,254 @@
+"""GPU parity: the sm_100a kernels through the C ABI against the CPU oracle.
+
+Bars (stated per test):
+  * dequant: bit-exact RNE_bf16(q * s) for every weight;
+  * KAT data (exact arithmetic): bit-exact outputs;
+  * seeded synthetic data: max relative error <= 1e-2 (denominator |ref| +
+    1e-6, crates/xnpu-cli/src/main.rs:2713) and mean absolute error <= 1e-3
+    against the oracle's f32-accumulated result before its final rounding,
+    plus the reference's golden tier |g - w| <= 0.01 + 0.01|w|
+    (main.rs:2705-2714).
+"""
+import json
+import struct
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from xnpu_b200 import hal, synth
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-2
+MAE = 1e-3
+
+
+def to_dev_u16(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint16).view(np.int16)).cuda().view(torch.bfloat16)
+
+
+def from_dev_bf16(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def import_planes(dev, q, s, **kw):
+    n, k = q.shape
+    src = synth.planes_bytes(synth.pack_codes_signed(q), s)
+    return hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, **kw))
+
+
+def rel_metrics(got, ref):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(got - ref)
+    return float((err / (np.abs(ref) + 1e-6)).max()), float(err.mean())
+
+
+def assert_parity(y_gpu_bits, y_ref_f32, what):
+    got = synth.bf16_bits_to_f32(y_gpu_bits)
+    max_rel, mae = rel_metrics(got, y_ref_f32)
+    ref_b = synth.bf16_bits_to_f32(O.round_bf16(y_ref_f32))
+    tier_ok = np.all(np.abs(got - ref_b) <= 0.01 + 0.01 * np.abs(ref_b))
+    assert max_rel <= MAX_REL and mae <= MAE and tier_ok, f"{what}: max_rel={max_rel:.3e} mae={mae:.3e}"
+
+
+# ------------------------------------------------------------------ dequant
+@pytest.mark.parametrize("n,k,tsi", [(4096, 4096, 16), (2048, 6144, 4), (256, 14336, 16)])
+def test_dequant_bit_exact_l1(dev, n, k, tsi):
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 21))
+    s = synth.synth_scales(n, k, 21)
+    pack = O.l1_pack(q, s, tsi=tsi)
+    w = hal.Weight.import_(dev, pack, hal.layout_desc(hal.XQ4_LAYOUT_L1, n, k, tsi=tsi, cols=8))
+    got = from_dev_bf16(hal.dequant(w))
+    torch.cuda.synchronize()
+    assert np.array_equal(got, O.l1_dequant(pack, n, k, tsi))
+
+
+@pytest.mark.parametrize("n,k", [(2048, 2048), (1024, 6144)])
+def test_dequant_bit_exact_l2(dev, n, k):
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 22))
+    s = synth.synth_scales(n, k, 22)
+    pack = O.l2_pack(q, s)
+    w = hal.Weight.import_(dev, pack, hal.layout_desc(hal.XQ4_LAYOUT_L2, n, k))
+    assert np.array_equal(from_dev_bf16(hal.dequant(w)), O.l2_dequant(pack, n, k))
+
+
+@pytest.mark.parametrize("n,k", [(1, 32), (17, 96), (333, 160), (4100, 4096)])
+def test_dequant_bit_exact_ragged(dev, n, k):
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 23))
+    s = synth.synth_scales(n, k, 23)
+    w = import_planes(dev, q, s)
+    assert np.array_equal(from_dev_bf16(hal.dequant(w)), O.dequant_planes(q, s))
+
+
+def test_dequant_full_range_scales(dev):
+    """Every nibble against scales of both signs, tiny and large magnitudes."""
+    n, k = 64, 512
+    rng = np.random.default_rng(24)
+    q = rng.integers(-8, 8, size=(n, k)).astype(np.int8)
+    sf = (rng.standard_normal((n, k // 32)) * 10.0 ** rng.integers(-30, 30, size=(n, k // 32))).astype(np.float32)
+    s = synth.f32_to_bf16_bits(sf)
+    w = import_planes(dev, q, s)
+    assert np.array_equal(from_dev_bf16(hal.dequant(w)), O.dequant_planes(q, s))
+
+
+# ------------------------------------------------------------------ KAT
+@pytest.mark.parametrize("n,k", [(2048, 2048), (256, 4096), (128, 14336)])
+def test_gemv_kat_bit_exact(dev, golden_dir, n, k):
+    raw = (golden_dir / f"kat_{n}x{k}.bin").read_bytes()
+    expect = np.frombuffer(raw, dtype="<u2", offset=8)
+    q, s, x = O.kat_fill(n, k)
+    if (n, k) == (2048, 2048):  # run-w4gemv default fixture geometry: tsi=1, 4 columns
+        w = hal.Weight.import_(dev, O.l1_pack(q, s, tsi=1, cols=4),
+                               hal.layout_desc(hal.XQ4_LAYOUT_L1, n, k, tsi=1, cols=4))
+    else:
+        w = import_planes(dev, q, s)
+    y = hal.linear(w, to_dev_u16(x[None, :]))
+    assert np.array_equal(from_dev_bf16(y)[0], expect)
+
+
+def test_gemv_kat_bit_exact_multi_token(dev, golden_dir):
+    """Every token of an m<=15 batch gets the exact KAT answer."""
+    n, k = 256, 4096
+    expect = np.frombuffer((golden_dir / f"kat_{n}x{k}.bin").read_bytes(), dtype="<u2", offset=8)
+    q, s, x = O.kat_fill(n, k)
+    w = import_planes(dev, q, s)
+    for m in (2, 8, 9, 15):
+        y = from_dev_bf16(hal.linear(w, to_dev_u16(np.repeat(x[None, :], m, axis=0))))
+        assert all(np.array_equal(y[t], expect) for t in range(m)), m
+
+
+# ------------------------------------------------------------------ goldens
+def test_gemv_reference_goldens(dev, golden_dir):
+    """Rows of the goldens written by the reference's own spot_rows, through
+    an L1 import and the GPU GEMV, within |g-w| <= 0.01+0.01|w|."""
+    man = json.loads((golden_dir / "manifest.json").read_text())["golden"]
+    for name, meta in sorted(man.items()):
+        raw = (golden_dir / f"golden_{name}.bin").read_bytes()
+        nrows, k = struct.unpack_from("<II", raw)
+        rows = np.frombuffer(raw, dtype="<u4", count=nrows, offset=8)
+        x = np.frombuffer(raw, dtype="<u2", count=k, offset=8 + 4 * nrows)
+        ref = synth.bf16_bits_to_f32(np.frombuffer(raw, dtype="<u2", count=nrows, offset=8 + 4 * nrows + 2 * k))
+        m, tsi, seed = meta["m"], meta["tsi"], meta["seed"]
+        q = synth.unpack_codes_signed(synth.synth_codes(m, k, seed))
+        s = synth.synth_scales(m, k, seed)
+        w = hal.Weight.import_(dev, O.l1_pack(q, s, tsi=tsi), hal.layout_desc(hal.XQ4_LAYOUT_L1, m, k, tsi=tsi, cols=8))
+        y = synth.bf16_bits_to_f32(from_dev_bf16(hal.linear(w, to_dev_u16(x[None, :])))[0])
+        g = y[rows]
+        assert np.all(np.abs(g - ref) <= 0.01 + 0.01 * np.abs(ref)), name
+        del w
+
+
+# ------------------------------------------------------------------ synthetic parity
+def oracle_rows(q, s, x, rows):
+    w = O.dequant_planes(q[rows], s[rows])
+    return O.gemv_bf16(w, x)
+
+
+def row_subset(n, limit=1536, seed=0):
+    if n <= limit:
+        return np.arange(n)
+    rng = np.random.default_rng(seed)
+    mid = rng.choice(np.arange(256, n - 256), size=limit - 512, replace=False)
+    return np.unique(np.concatenate([np.arange(256), mid, np.arange(n - 256, n)]))
+
+
+LLAMA8B = {"qkv": (6144, 4096), "o": (4096, 4096), "gate": (14336, 4096), "up": (14336, 4096),
+           "down": (4096, 14336)}
+
+
+@pytest.mark.parametrize("name", sorted(LLAMA8B))
+def test_gemv_parity_8b_shapes(dev, name):
+    """One layer of the 8B-shaped decode linear set at m=1 (and 4096x4096:
+    the single-GEMV configuration)."""
+    n, k = LLAMA8B[name]
+    seed = 100 + sorted(LLAMA8B).index(name)
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, seed))
+    s = synth.synth_scales(n, k, seed)
+    x = synth.synth_x(1, k, seed)
+    w = import_planes(dev, q, s)
+    y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
+    rows = row_subset(n)
+    assert_parity(y[:, rows], oracle_rows(q, s, x, rows), name)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 9, 12, 15])
+def test_gemv_parity_batch_sweep(dev, m):
+    """4096 -> 14336 gate projection, the decode batch sweep below m=16."""
+    n, k = 14336, 4096
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 200))
+    s = synth.synth_scales(n, k, 200)
+    x = synth.synth_x(m, k, 200 + m)
+    w = import_planes(dev, q, s)
+    y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
+    rows = row_subset(n, limit=768)
+    assert_parity(y[:, rows], oracle_rows(q, s, x, rows), f"m={m}")
+
+
+@pytest.mark.parametrize("n,k,m", [(1, 32, 1), (17, 96, 3), (333, 160, 8), (4100, 4128, 2), (40, 14336, 11)])
+def test_gemv_parity_ragged(dev, n, k, m):
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 300 + n))
+    s = synth.synth_scales(n, k, 300 + n)
+    x = synth.synth_x(m, k, 301 + n)
+    w = import_planes(dev, q, s)
+    y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
+    assert_parity(y, oracle_rows(q, s, x, np.arange(n)), f"{n}x{k} m={m}")
+
+
+def test_gemv_f32_output(dev):
+    """lm_head-style f32 logits (no final rounding)."""
+    n, k = 4096, 4096
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 400))
+    s = synth.synth_scales(n, k, 400)
+    x = synth.synth_x(1, k, 400)
+    w = import_planes(dev, q, s)
+    y = hal.linear(w, to_dev_u16(x), out_dtype=torch.float32).cpu().numpy()
+    ref = oracle_rows(q, s, x, np.arange(n))
+    max_rel, mae = rel_metrics(y, ref)
+    assert max_rel <= MAX_REL and mae <= MAE, (max_rel, mae)
+    # argmax / top-8 / rel_rms gate of the reference's lm_head check (main.rs:4059-4097)
+    assert int(np.argmax(y[0])) == int(np.argmax(ref[0]))
+    assert len(set(np.argsort(-y[0])[:8]) & set(np.argsort(-ref[0])[:8])) == 8
+    rel_rms = np.sqrt(np.mean((y - ref) ** 2)) / max(np.sqrt(np.mean(ref ** 2)), 1e-9)
+    assert rel_rms < 0.05
+
+
+def test_output_guard_band(dev):
+    """The kernel writes exactly m*n outputs: canaries around y stay intact."""
+    n, k, m = 333, 160, 3
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 500))
+    s = synth.synth_scales(n, k, 500)
+    w = import_planes(dev, q, s)
+    x = to_dev_u16(synth.synth_x(m, k, 500))
+    pad = 64
+    buf = torch.full((m * n + 2 * pad,), 12345.0, dtype=torch.bfloat16, device="cuda")
+    out = buf[pad:pad + m * n].view(m, n)
+    # out must be 16-byte aligned: pad*2 = 128 bytes keeps the allocation's alignment
+    hal.linear(w, x, out=out)
+    torch.cuda.synchronize()
+    b = buf.float().cpu().numpy()
+    assert np.all(b[:pad] == 12345.0) and np.all(b[pad + m * n:] == 12345.0)
+
+
+# ------------------------------------------------------------------ HAL path
+def test_hal_buffer_op_timeline(dev):
+    """The reference-shaped call sequence: buffers, op submit, timeline wait."""
+    n, k, m = 4096, 4096, 1
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 600))
+    s = synth.synth_scales(n, k, 600)
+    x = synth.synth_x(m, k, 600)
+    w = hal.Weight.import_(dev, O.l1_pack(q, s, tsi=16), hal.layout_desc(hal.XQ4_LAYOUT_L1, n, k, tsi=16, cols=8))
+    xb = hal.BufferObject.new(dev, m * k * 2)
+    yb = hal.BufferObject.new(dev, m * n * 2)
+    xb.write(0, x)
+    seqs = [hal.LinearOp(w, xb, yb, m).submit(dev) for _ in range(3)]
+    assert seqs == sorted(seqs) and seqs[-1] == dev.last_seq()
+    hal.timeline_wait(dev, seqs[-1], 10_000_000_000)
+    y = np.frombuffer(yb.read(0, m * n * 2), dtype=np.uint16).reshape(m, n)
+    assert_parity(y, oracle_rows(q, s, x, np.arange(n)), "hal")
+    with pytest.raises(hal.Xq4Error):
+        hal.timeline_wait(dev, seqs[-1] + 5, 1000)  # never submitted
+    with pytest.raises(hal.Xq4Error):
+        hal.LinearOp(w, xb, yb, m + 1).submit(dev)  # x buffer too small for m=2

@@ -1,0 +1,367 @@
+// api.cu -- the C ABI (include/xq4.h): devices, buffers, weights, the linear
+// op and the timeline wait.  Mirrors the reference HAL's operator surface
+// (crates/xnpu-hal/src/{accel,bo,hwctx,ert}.rs) over CUDA.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <time.h>
+#include <unistd.h>
+#include <new>
+#include <vector>
+
+#include "xq4_internal.h"
+#include "xq4_layout.h"
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[512];
+
+int xq4_fail(int code, const char *fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+void xq4_clear_error(void) { g_err[0] = 0; }
+
+static int cuda_fail(cudaError_t e, const char *what)
+{
+    return xq4_fail(XQ4_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CK(call, what)                                \
+    do {                                              \
+        cudaError_t e_ = (call);                      \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+extern "C" const char *xq4_last_error_string(void) { return g_err; }
+extern "C" const char *xq4_version(void) { return "xq4 0.1 (sm_100a)"; }
+
+// ------------------------------------------------------------------ device
+namespace {
+constexpr int kRing = 256;  // timeline points kept as live events
+}
+
+struct xq4_device {
+    int ordinal;
+    cudaStream_t stream;
+    cudaEvent_t ring[kRing];
+    uint64_t last_seq;      // newest submitted point (0 = none)
+    uint64_t done_seq;      // newest point known complete
+    cudaDeviceProp prop;
+};
+
+cudaStream_t xq4_device_cuda_stream(xq4_device *dev) { return dev->stream; }
+int xq4_device_ordinal(const xq4_device *dev) { return dev->ordinal; }
+
+extern "C" int xq4_device_open(int ordinal, xq4_device **out)
+{
+    xq4_clear_error();
+    if (!out) return xq4_fail(XQ4_EINVAL, "out is NULL");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0)
+        return xq4_fail(XQ4_ENODEV, "no CUDA device (%s)", e == cudaSuccess ? "count 0" : cudaGetErrorString(e));
+    if (ordinal < 0 || ordinal >= count)
+        return xq4_fail(XQ4_ENODEV, "device ordinal %d out of range [0, %d)", ordinal, count);
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, ordinal), "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return xq4_fail(XQ4_ENODEV, "device %d is sm_%d%d; this library is built for sm_100a only", ordinal,
+                        prop.major, prop.minor);
+    CK(cudaSetDevice(ordinal), "cudaSetDevice");
+    xq4_device *d = new (std::nothrow) xq4_device();
+    if (!d) return xq4_fail(XQ4_ENOMEM, "host allocation");
+    d->ordinal = ordinal;
+    d->prop = prop;
+    cudaError_t ce = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) {
+        delete d;
+        return cuda_fail(ce, "cudaStreamCreate");
+    }
+    for (int i = 0; i < kRing; i++) {
+        ce = cudaEventCreateWithFlags(&d->ring[i], cudaEventDisableTiming);
+        if (ce != cudaSuccess) {
+            for (int j = 0; j < i; j++) cudaEventDestroy(d->ring[j]);
+            cudaStreamDestroy(d->stream);
+            delete d;
+            return cuda_fail(ce, "cudaEventCreate");
+        }
+    }
+    *out = d;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_device_close(xq4_device *dev)
+{
+    xq4_clear_error();
+    if (!dev) return XQ4_OK;
+    cudaSetDevice(dev->ordinal);
+    cudaError_t e = cudaStreamSynchronize(dev->stream);
+    for (int i = 0; i < kRing; i++) cudaEventDestroy(dev->ring[i]);
+    cudaStreamDestroy(dev->stream);
+    delete dev;
+    if (e != cudaSuccess) return cuda_fail(e, "draining the device queue at close");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_device_query(const xq4_device *dev, xq4_device_info *info)
+{
+    xq4_clear_error();
+    if (!dev || !info) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    memset(info, 0, sizeof *info);
+    info->ordinal = dev->ordinal;
+    info->sm_count = dev->prop.multiProcessorCount;
+    info->cc_major = dev->prop.major;
+    info->cc_minor = dev->prop.minor;
+    info->hbm_bytes = dev->prop.totalGlobalMem;
+    info->l2_bytes = (size_t)dev->prop.l2CacheSize;
+    snprintf(info->name, sizeof info->name, "%.95s", dev->prop.name);
+    return XQ4_OK;
+}
+
+extern "C" void *xq4_device_stream(xq4_device *dev) { return dev ? (void *)dev->stream : nullptr; }
+
+// ------------------------------------------------------------------ buffers
+struct xq4_buffer {
+    xq4_device *dev;
+    void *ptr;
+    size_t bytes;
+};
+
+extern "C" int xq4_buffer_create(xq4_device *dev, size_t bytes, xq4_buffer **out)
+{
+    xq4_clear_error();
+    if (!dev || !out) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    *out = nullptr;
+    if (bytes == 0) return xq4_fail(XQ4_EINVAL, "zero-size buffer");
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    }
+    xq4_buffer *b = new (std::nothrow) xq4_buffer{dev, p, bytes};
+    if (!b) {
+        cudaFree(p);
+        return xq4_fail(XQ4_ENOMEM, "host allocation");
+    }
+    *out = b;
+    return XQ4_OK;
+}
+
+static int check_range(const xq4_buffer *buf, size_t off, size_t len)
+{
+    if (off > buf->bytes || len > buf->bytes - off)
+        return xq4_fail(XQ4_EINVAL, "range [%zu, %zu) outside buffer of %zu bytes", off, off + len, buf->bytes);
+    return XQ4_OK;
+}
+
+extern "C" int xq4_buffer_upload(xq4_buffer *buf, const void *host, size_t offset, size_t len)
+{
+    xq4_clear_error();
+    if (!buf || (!host && len)) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (int rc = check_range(buf, offset, len)) return rc;
+    if (!len) return XQ4_OK;
+    CK(cudaSetDevice(buf->dev->ordinal), "cudaSetDevice");
+    CK(cudaMemcpyAsync((char *)buf->ptr + offset, host, len, cudaMemcpyHostToDevice, buf->dev->stream),
+       "upload");
+    CK(cudaStreamSynchronize(buf->dev->stream), "upload sync");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_buffer_download(xq4_buffer *buf, void *host, size_t offset, size_t len)
+{
+    xq4_clear_error();
+    if (!buf || (!host && len)) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (int rc = check_range(buf, offset, len)) return rc;
+    if (!len) return XQ4_OK;
+    CK(cudaSetDevice(buf->dev->ordinal), "cudaSetDevice");
+    CK(cudaMemcpyAsync(host, (const char *)buf->ptr + offset, len, cudaMemcpyDeviceToHost, buf->dev->stream),
+       "download");
+    CK(cudaStreamSynchronize(buf->dev->stream), "download sync");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_buffer_destroy(xq4_buffer *buf)
+{
+    xq4_clear_error();
+    if (!buf) return XQ4_OK;
+    cudaSetDevice(buf->dev->ordinal);
+    cudaStreamSynchronize(buf->dev->stream);  // no queued op may still use it
+    cudaError_t e = cudaFree(buf->ptr);
+    delete buf;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
+    return XQ4_OK;
+}
+
+extern "C" void *xq4_buffer_device_ptr(const xq4_buffer *buf) { return buf ? buf->ptr : nullptr; }
+extern "C" size_t xq4_buffer_size(const xq4_buffer *buf) { return buf ? buf->bytes : 0; }
+
+// ------------------------------------------------------------------ weights
+extern "C" int xq4_weight_import(xq4_device *dev, const void *src, size_t src_len,
+                                 const xq4_layout_desc *desc, xq4_weight **out)
+{
+    xq4_clear_error();
+    if (!dev || !src || !out) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    *out = nullptr;
+    int r0, r1;
+    if (int rc = xq4_check_desc(desc, src_len, &r0, &r1)) return rc;
+    const int n = r1 - r0, k = desc->k;
+    const size_t bytes = xq4g_bytes(n, k);
+    std::vector<uint8_t> host;
+    try {
+        host.resize(bytes);
+    } catch (...) {
+        return xq4_fail(XQ4_ENOMEM, "host staging of %zu bytes", bytes);
+    }
+    if (int rc = xq4_repack_rows(src, src_len, desc, r0, r1, host.data())) return rc;
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for weight: %s", bytes, cudaGetErrorString(e));
+    }
+    e = cudaMemcpyAsync(p, host.data(), bytes, cudaMemcpyHostToDevice, dev->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(dev->stream);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "weight upload");
+    }
+    xq4_weight *w = new (std::nothrow) xq4_weight();
+    if (!w) {
+        cudaFree(p);
+        return xq4_fail(XQ4_ENOMEM, "host allocation");
+    }
+    w->dev = dev;
+    w->n = n;
+    w->k = k;
+    w->nb = xq4g_nb(n);
+    w->kc = xq4g_kc(k);
+    w->d_pack = (uint8_t *)p;
+    w->bytes = bytes;
+    *out = w;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_weight_destroy(xq4_weight *w)
+{
+    xq4_clear_error();
+    if (!w) return XQ4_OK;
+    cudaSetDevice(w->dev->ordinal);
+    cudaStreamSynchronize(w->dev->stream);
+    cudaError_t e = cudaFree(w->d_pack);
+    delete w;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_weight_shape(const xq4_weight *w, int *n, int *k, size_t *device_bytes)
+{
+    xq4_clear_error();
+    if (!w) return xq4_fail(XQ4_EINVAL, "NULL weight");
+    if (n) *n = w->n;
+    if (k) *k = w->k;
+    if (device_bytes) *device_bytes = w->bytes;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream)
+{
+    xq4_clear_error();
+    if (!w || !out_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if ((uintptr_t)out_dev & 15) return xq4_fail(XQ4_EINVAL, "output must be 16-byte aligned");
+    CK(cudaSetDevice(w->dev->ordinal), "cudaSetDevice");
+    cudaStream_t st = stream ? (cudaStream_t)stream : w->dev->stream;
+    CK(xq4_launch_dequant(w->d_pack, w->n, w->k, out_dev, st), "dequant launch");
+    return XQ4_OK;
+}
+
+// ------------------------------------------------------------------ linear
+static int launch_linear(const xq4_weight *w, const void *x, void *y, int m, int out_dtype, cudaStream_t st)
+{
+    if (m <= 0) return xq4_fail(XQ4_EINVAL, "m must be >= 1 (got %d)", m);
+    if (out_dtype != XQ4_OUT_BF16 && out_dtype != XQ4_OUT_F32)
+        return xq4_fail(XQ4_EINVAL, "unknown out_dtype %d", out_dtype);
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 15))
+        return xq4_fail(XQ4_EINVAL, "x and y must be 16-byte aligned");
+    const int f32 = out_dtype == XQ4_OUT_F32;
+    cudaError_t e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x, m, y, f32, st)
+                           : xq4_launch_gemm(w->d_pack, w->n, w->k, x, m, y, f32, st);
+    if (e != cudaSuccess) return cuda_fail(e, m < 16 ? "gemv launch" : "gemm launch");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_linear(xq4_device *dev, const xq4_weight *w, const xq4_buffer *x_buf, size_t x_off,
+                          xq4_buffer *y_buf, size_t y_off, int m, int out_dtype, uint64_t *seq)
+{
+    xq4_clear_error();
+    if (!dev || !w || !x_buf || !y_buf) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (w->dev != dev || x_buf->dev != dev || y_buf->dev != dev)
+        return xq4_fail(XQ4_EINVAL, "weight and buffers must belong to this device");
+    if (m <= 0) return xq4_fail(XQ4_EINVAL, "m must be >= 1 (got %d)", m);
+    const size_t xb = (size_t)m * w->k * 2, yb = (size_t)m * w->n * (out_dtype == XQ4_OUT_F32 ? 4 : 2);
+    if (int rc = check_range(x_buf, x_off, xb)) return rc;
+    if (int rc = check_range(y_buf, y_off, yb)) return rc;
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    int rc = launch_linear(w, (const char *)x_buf->ptr + x_off, (char *)y_buf->ptr + y_off, m, out_dtype,
+                           dev->stream);
+    if (rc) return rc;
+    const uint64_t s = dev->last_seq + 1;
+    CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");
+    dev->last_seq = s;
+    if (seq) *seq = s;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev, int m, int out_dtype,
+                              void *stream)
+{
+    xq4_clear_error();
+    if (!w || !x_dev || !y_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    cudaStream_t st = stream ? (cudaStream_t)stream : w->dev->stream;
+    return launch_linear(w, x_dev, y_dev, m, out_dtype, st);
+}
+
+static uint64_t now_ns()
+{
+    timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (uint64_t)ts.tv_sec * 1000000000ull + ts.tv_nsec;
+}
+
+extern "C" int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns)
+{
+    xq4_clear_error();
+    if (!dev) return xq4_fail(XQ4_EINVAL, "NULL device");
+    if (seq > dev->last_seq) return xq4_fail(XQ4_EINVAL, "seq %llu was never submitted (last %llu)",
+                                             (unsigned long long)seq, (unsigned long long)dev->last_seq);
+    if (seq <= dev->done_seq) return XQ4_OK;
+    // An evicted point is covered by the oldest live one (in-order queue).
+    uint64_t probe = seq;
+    if (dev->last_seq >= (uint64_t)kRing && seq <= dev->last_seq - kRing) probe = dev->last_seq - kRing + 1;
+    cudaEvent_t ev = dev->ring[probe % kRing];
+    const uint64_t t0 = now_ns();
+    unsigned spins = 0;
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) {
+            if (probe > dev->done_seq) dev->done_seq = probe;
+            return XQ4_OK;
+        }
+        if (e != cudaErrorNotReady) return cuda_fail(e, "timeline wait");
+        if (timeout_ns >= 0 && (int64_t)(now_ns() - t0) >= timeout_ns)
+            return xq4_fail(XQ4_ETIMEDOUT, "seq %llu not complete after %lld ns", (unsigned long long)seq,
+                            (long long)timeout_ns);
+        if (++spins > 64) usleep(20);
+    }
+}
+
+extern "C" uint64_t xq4_last_seq(const xq4_device *dev) { return dev ? dev->last_seq : 0; }

@@ -1,0 +1,170 @@
+// comm.cu -- column-sharded linear: each GPU owns n/P output rows of W, runs
+// the local GEMV/GEMM into its slice and an NCCL all-gather (NVLink/NVSwitch)
+// reassembles the full output on every rank.
+//
+// The reference is single-device; its nearest counterpart is the row split of
+// one projection over 8 AIE columns and the host gather of the per-column C
+// sections (crates/xnpu-cli/src/main.rs:2186-2191, w4u_read_c :3066-3091).
+//
+// NCCL is bound at run time (dlopen of libnccl.so.2): in a process that has
+// already loaded torch this resolves to torch's NCCL, so both share one
+// library, and the rest of libxq4 works on machines without NCCL.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
+#include <new>
+#include <string.h>
+
+#include "xq4_internal.h"
+
+namespace {
+
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *);
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    const char *(*GetErrorString)(ncclResult_t);
+    bool ok;
+};
+
+NcclApi *nccl_api()
+{
+    static NcclApi api = [] {
+        NcclApi a{};
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return a;
+        a.GetUniqueId = (decltype(a.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        a.CommInitRank = (decltype(a.CommInitRank))dlsym(h, "ncclCommInitRank");
+        a.CommDestroy = (decltype(a.CommDestroy))dlsym(h, "ncclCommDestroy");
+        a.AllGather = (decltype(a.AllGather))dlsym(h, "ncclAllGather");
+        a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
+        a.ok = a.GetUniqueId && a.CommInitRank && a.CommDestroy && a.AllGather && a.GetErrorString;
+        return a;
+    }();
+    return &api;
+}
+
+int nccl_fail(ncclResult_t r, const char *what)
+{
+    NcclApi *a = nccl_api();
+    return xq4_fail(XQ4_ENCCL, "%s: %s", what, a->ok ? a->GetErrorString(r) : "NCCL unavailable");
+}
+
+// ws[p][t][j] -> y[t][p*ns + j]  (rank-major all-gather result -> token-major)
+template <typename T>
+__global__ void shard_permute(const T *__restrict__ ws, T *__restrict__ y, int nranks, int m, int ns)
+{
+    const size_t total = (size_t)nranks * m * ns;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t j = i % ns;
+        const size_t rest = i / ns;
+        const size_t t = rest % m, p = rest / m;
+        y[t * ((size_t)nranks * ns) + p * ns + j] = ws[i];
+    }
+}
+
+}  // namespace
+
+struct xq4_comm {
+    xq4_device *dev;
+    ncclComm_t nccl;
+    int rank, nranks;
+};
+
+extern "C" int xq4_comm_unique_id(void *id_out)
+{
+    xq4_clear_error();
+    if (!id_out) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    static_assert(sizeof(ncclUniqueId) == XQ4_UNIQUE_ID_BYTES, "unique id size");
+    NcclApi *a = nccl_api();
+    if (!a->ok) return xq4_fail(XQ4_ENCCL, "libnccl.so.2 could not be loaded: %s", dlerror());
+    ncclUniqueId id;
+    ncclResult_t r = a->GetUniqueId(&id);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+    memcpy(id_out, &id, sizeof id);
+    return XQ4_OK;
+}
+
+extern "C" int xq4_comm_init(xq4_device *dev, int rank, int nranks, const void *unique_id, xq4_comm **out)
+{
+    xq4_clear_error();
+    if (!dev || !unique_id || !out) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    *out = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks)
+        return xq4_fail(XQ4_EINVAL, "rank %d / nranks %d invalid", rank, nranks);
+    NcclApi *a = nccl_api();
+    if (!a->ok) return xq4_fail(XQ4_ENCCL, "libnccl.so.2 could not be loaded");
+    cudaError_t e = cudaSetDevice(xq4_device_ordinal(dev));
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof id);
+    ncclComm_t c;
+    ncclResult_t r = a->CommInitRank(&c, nranks, id, rank);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+    xq4_comm *cm = new (std::nothrow) xq4_comm{dev, c, rank, nranks};
+    if (!cm) {
+        a->CommDestroy(c);
+        return xq4_fail(XQ4_ENOMEM, "host allocation");
+    }
+    *out = cm;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_comm_destroy(xq4_comm *comm)
+{
+    xq4_clear_error();
+    if (!comm) return XQ4_OK;
+    NcclApi *a = nccl_api();
+    cudaSetDevice(xq4_device_ordinal(comm->dev));
+    ncclResult_t r = a->CommDestroy(comm->nccl);
+    delete comm;
+    if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w, const void *x_dev, void *y_full_dev,
+                                  void *ws_dev, int m, int out_dtype, void *stream)
+{
+    xq4_clear_error();
+    if (!comm || !w || !x_dev || !y_full_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (m <= 0) return xq4_fail(XQ4_EINVAL, "m must be >= 1 (got %d)", m);
+    if (out_dtype != XQ4_OUT_BF16 && out_dtype != XQ4_OUT_F32)
+        return xq4_fail(XQ4_EINVAL, "unknown out_dtype %d", out_dtype);
+    if (m > 1 && !ws_dev) return xq4_fail(XQ4_EINVAL, "m > 1 needs a workspace");
+    const size_t esz = out_dtype == XQ4_OUT_F32 ? 4 : 2;
+    const int ns = w->n;
+    if ((ns * esz) % 16)
+        return xq4_fail(XQ4_EINVAL, "shard rows (%d) x element size must be a multiple of 16 bytes", ns);
+    if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_full_dev & 15) || ((uintptr_t)ws_dev & 15))
+        return xq4_fail(XQ4_EINVAL, "x, y and ws must be 16-byte aligned");
+    NcclApi *a = nccl_api();
+    if (!a->ok) return xq4_fail(XQ4_ENCCL, "libnccl.so.2 could not be loaded");
+    cudaError_t e = cudaSetDevice(xq4_device_ordinal(comm->dev));
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    cudaStream_t st = stream ? (cudaStream_t)stream : xq4_device_cuda_stream(comm->dev);
+    const int f32 = out_dtype == XQ4_OUT_F32;
+    const ncclDataType_t dt = f32 ? ncclFloat32 : ncclBfloat16;
+    const size_t slice = (size_t)m * ns;  // elements per rank
+    char *gather = (char *)(m == 1 ? y_full_dev : ws_dev);
+    void *mine = gather + (size_t)comm->rank * slice * esz;
+    e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st)
+               : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
+    ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    if (m > 1) {
+        const size_t total = slice * comm->nranks;
+        const unsigned blocks = (unsigned)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+        if (f32)
+            shard_permute<float><<<blocks, 256, 0, st>>>((const float *)ws_dev, (float *)y_full_dev,
+                                                         comm->nranks, m, ns);
+        else
+            shard_permute<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)ws_dev, (uint16_t *)y_full_dev,
+                                                            comm->nranks, m, ns);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard permute: %s", cudaGetErrorString(e));
+    }
+    return XQ4_OK;
+}

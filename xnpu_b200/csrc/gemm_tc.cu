@@ -1,0 +1,9 @@
+// gemm_tc.cu -- K2: batched-decode / prefill dequant-GEMM (m >= 16).
+#include <cuda_runtime.h>
+#include "xq4_internal.h"
+
+cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y, int out_f32,
+                            cudaStream_t st)
+{
+    return xq4_launch_gemv(pack, n, k, x, m, y, out_f32, st);
+}

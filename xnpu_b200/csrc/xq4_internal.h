@@ -1,0 +1,41 @@
+// xq4_internal.h -- private declarations shared by the libxq4 translation units.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+#include "../../include/xq4.h"
+
+// Record a failure message for xq4_last_error_string() and return `code`.
+int xq4_fail(int code, const char *fmt, ...)
+#if defined(__GNUC__)
+    __attribute__((format(printf, 2, 3)))
+#endif
+    ;
+void xq4_clear_error(void);
+
+// repack.cpp
+int xq4_check_desc(const xq4_layout_desc *desc, size_t src_len, int *r0, int *r1);
+int xq4_repack_rows(const void *src, size_t src_len, const xq4_layout_desc *desc, int r0, int r1,
+                    uint8_t *dst);
+
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+
+// A weight resident in HBM, in XQ4G layout.
+struct xq4_weight {
+    struct xq4_device *dev;
+    int n, k;          // logical rows / reduction length
+    int nb, kc;        // row blocks, 64-K chunks
+    uint8_t *d_pack;   // xq4g_bytes(n, k) bytes
+    size_t bytes;
+};
+
+// Kernel launchers (gemv.cu, gemm_tc.cu, dequant.cu).  All return cudaError_t
+// of the launch; arguments are validated by the callers in api.cu.
+cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
+                            int out_f32, cudaStream_t st);
+cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
+                            int out_f32, cudaStream_t st);
+cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);
+cudaStream_t xq4_device_cuda_stream(struct xq4_device *dev);
+int xq4_device_ordinal(const struct xq4_device *dev);
+#endif
