@@ -203,7 +203,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="xq4", choices=["xq4", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=32,
+                    help="layers of the weight set (32 = the benchmark; fewer only for profiler captures)")
+    ap.add_argument("--skip-e2e", action="store_true", help="profiler captures only")
+    ap.add_argument("--skip-lmhead", action="store_true", help="profiler captures only")
     args = ap.parse_args()
+    global LAYERS
+    LAYERS = args.layers
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -263,21 +269,28 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # warm-up
+    # warm-up (eager), then capture one step into a CUDA graph: 160 launches
+    # per token are too many to issue from the host at HBM speed
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step(sp)
     barrier()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        per_step = step(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    barrier()
 
-    # device-timed steps (inputs resident in HBM)
+    # device-timed steps (inputs resident in HBM), graph replays
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches = 0
     with ClockSampler(local) as clk:
         barrier()
         ev0.record(stream)
         with torch.cuda.stream(stream):
             for _ in range(args.steps):
-                launches += step(sp)
+                graph.replay()
         ev1.record(stream)
         barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
@@ -286,8 +299,19 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     clocks = clk.summary()
+    launches = per_step * args.steps
 
-    # per-launch kernel durations for the roofline (events around each launch)
+    # roofline: algorithmic bytes of every GEMV launch in the timed region
+    # (per GPU) over the timed region's duration
+    gpu_step_bytes = 0
+    for name, n, k in SHAPES:
+        ns = n // world if (world > 1 and name in ("gate", "up")) else n
+        gpu_step_bytes += algo_bytes(ns, k) * LAYERS
+    achieved = gpu_step_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # isolated single-launch durations per shape (events around each launch;
+    # includes launch latency) -- diagnostic detail only
     per = {name: [] for name, _, _ in SHAPES}
     evs = []
     with torch.cuda.stream(stream):
@@ -295,29 +319,19 @@ def main():
             for name, n, k in SHAPES:
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                if comm is not None and name in ("gate", "up"):
-                    check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
-                else:
-                    check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
+                check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
                 b.record(stream)
                 evs.append((name, a, b))
     torch.cuda.synchronize()
     for name, a, b in evs:
         per[name].append(a.elapsed_time(b))
-    tot_bytes = 0
-    tot_ms = 0.0
-    for name, n, k in SHAPES:
-        ns = n // world if (world > 1 and name in ("gate", "up")) else n
-        tot_bytes += algo_bytes(ns, k) * len(per[name])
-        tot_ms += sum(per[name])
-    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
-    peak, peak_kind = measured_peaks()
+    del graph
 
     # end-to-end through the C ABI with host buffers (pinned), copies inside
-    e2e = e2e_run(dev, weights, comm, world, args)
+    e2e = None if args.skip_e2e else e2e_run(dev, weights, comm, world, args)
 
     # lm_head (sharded the same way), f32 logits
-    lm = lmhead_run(dev, rank, world, comm, L, stream)
+    lm = None if args.skip_lmhead else lmhead_run(dev, rank, world, comm, L, stream)
 
     step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
     if rank == 0:
@@ -338,7 +352,8 @@ def main():
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "gemv_kernel<1> (decode GEMV, m=1)",
                          "traffic": None,
-                         "per_shape_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()}},
+                         "region": "all GEMV launches of the timed steps (CUDA graph replays)",
+                         "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()}},
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,

@@ -13,7 +13,9 @@
  * Ownership: every handle is created by one call and released by exactly one
  * destroy/close call (the reference's RAII: Device owns fd + heap,
  * crates/xnpu-hal/src/accel.rs:107-116; BufferObject closes its handle on drop,
- * crates/xnpu-hal/src/bo.rs:160-181).  Handles are not thread-safe; use one
+ * crates/xnpu-hal/src/bo.rs:160-181).  A weight or buffer may be destroyed
+ * after its device was closed, but no op may use it after that.  Handles are
+ * not thread-safe; use one
  * device handle (one in-order queue) per thread, as the reference does
  * (one in-order queue per context, crates/xnpu-cli/src/main.rs:1637-1641).
  *
@@ -147,7 +149,8 @@ int xq4_repack_host(const void *src, size_t src_len, const xq4_layout_desc *desc
                     void *dst, size_t dst_len);
 
 /* Dequantize the whole weight to bf16, row-major [n][k], into device memory
- * at out_dev (n*k*2 bytes), on `stream` (NULL = the weight's device stream).
+ * at out_dev (n*k*2 bytes), on `stream` (a cudaStream_t; NULL = CUDA's
+ * default stream, as in the CUDA API).
  * Restates w4u_row_bf16 (crates/xnpu-cli/src/main.rs:3102-3125) for every row. */
 int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream);
 
@@ -164,7 +167,8 @@ int xq4_linear(xq4_device *dev, const xq4_weight *w,
                int m, int out_dtype, uint64_t *seq);
 
 /* Same op on raw device pointers and a caller stream (a cudaStream_t; NULL =
- * the weight's device stream).  x and y must be 16-byte aligned. */
+ * CUDA's default stream, as in the CUDA API; the device queue of xq4_linear
+ * is xq4_device_stream()).  x and y must be 16-byte aligned. */
 int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev,
                    int m, int out_dtype, void *stream);
 
@@ -177,6 +181,12 @@ int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev,
 int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns);
 /* Timeline point of the newest submitted op. */
 uint64_t xq4_last_seq(const xq4_device *dev);
+/* Read and clear the device's pipeline-fault bits.  Every wait inside the
+ * kernels is bounded; a kernel whose wait runs out (a pipeline that stopped
+ * making progress) sets a bit here and returns instead of hanging the GPU.
+ * The reference's counterpart is the firmware health-data / ERT state check
+ * (crates/xnpu-hal/src/ert.rs:147-165).  *bits = 0 means no fault. */
+int xq4_device_fault(xq4_device *dev, uint32_t *bits);
 
 /* ---------------------------------------------------------------- shards */
 /* Column (N) sharding of large-N projections over P GPUs with an NCCL
@@ -193,7 +203,7 @@ int xq4_comm_destroy(xq4_comm *comm);
  * every rank).  Computes the local slice, all-gathers the slices over NCCL and
  * leaves the full output on every rank.  y_full needs m*n_shard*nranks
  * elements of out_dtype; ws (scratch of the same size) may be NULL when
- * m == 1. */
+ * m == 1.  Runs on `stream` (a cudaStream_t; NULL = CUDA's default stream). */
 int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w_shard,
                        const void *x_dev, void *y_full_dev, void *ws_dev,
                        int m, int out_dtype, void *stream);

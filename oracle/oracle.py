@@ -36,6 +36,7 @@ _SIGS = {
     "q4o_gemv_bf16": (_I, [_u16p, _u16p, _I, _I, _I, _f32p, _I]),
     "q4o_gemv_l1": (_I, [_u8p, _I, _I, _I, _I, _I, _u16p, _I, _f32p, _I]),
     "q4o_gemv_l2": (_I, [_u8p, _I, _I, _u16p, _I, _f32p, _I]),
+    "q4o_gemv_q": (_I, [_i8p, _u16p, _I, _I, _u16p, _I, _f32p, _I]),
     "q4o_round_bf16": (None, [_f32p, _SZ, _u16p]),
     "q4o_kat_fill": (None, [_I, _I, _I, _i8p, _u16p, _u16p]),
     "q4o_kat_ref": (None, [_I, _I, _I, _u16p]),
@@ -179,6 +180,19 @@ def gemv_l2(pack, n, k, x, nthreads=8):
     m = x.shape[0]
     y = np.empty((m, n), dtype=np.float32)
     _ok(lib().q4o_gemv_l2(_p(pack, _u8p), n, k, _p(x, _u16p), m, _p(y, _f32p), nthreads), "gemv_l2")
+    return y
+
+
+def gemv_q(q, s, x, nthreads=8):
+    """f32 y[m][n] (before the final RNE) of the reference's GEMV
+    (main.rs:2287-2296): w = f32(q) * f32(s) unrounded, sequential f32 sum."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(s, dtype=np.uint16)
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    n, k = q.shape
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _ok(lib().q4o_gemv_q(_p(q, _i8p), _p(s, _u16p), n, k, _p(x, _u16p), m, _p(y, _f32p), nthreads), "gemv_q")
     return y
 
 

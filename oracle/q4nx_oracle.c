@@ -303,16 +303,24 @@ int q4o_l2_row_ref(const uint8_t *pack, int m, int k, int row, uint16_t *out)
 
 /* --------------------------------------------------------- GEMV reference
  *
- * y[m][i] = sum_k f32(w[i][k]) * f32(x[m][k]), accumulated sequentially over k
- * in f32 (crates/xnpu-cli/src/main.rs:2287-2296; tools/w4_import.py:55-63 for
- * real weights), returned in f32 BEFORE the final RNE so callers can compare
- * against the unrounded value; q4o_f32_to_bf16 gives the reference's output.
+ * y[m][i] = sum_k w[i][k] * f32(x[m][k]), accumulated sequentially over k in
+ * f32 and returned in f32 BEFORE the final RNE so callers can compare against
+ * the unrounded value; q4o_f32_to_bf16 gives the reference's output.
+ *   - over a packed layout or q/s planes, w = f32(q) * f32(scale) exactly, with
+ *     no bf16 rounding of w: the reference's GEMV host reference,
+ *     crates/xnpu-cli/src/main.rs:2287-2296 (`let w = nibble as f32 *
+ *     scale; acc += w * bf16_to_f32(x)`);
+ *   - over dequantized bf16 weights (q4o_gemv_bf16), w = the bf16 value: the
+ *     importer's golden rows, tools/w4_import.py:55-63 (f32 matmul of the
+ *     dequantized weights).
  * Rows are independent; threads split rows, each row keeps the reference's
  * sequential order, so the result does not depend on the thread count.
  */
 typedef struct {
-    int kind; /* 0: dequantized bf16 w; 1: L1 pack; 2: L2 pack */
+    int kind; /* 0: dequantized bf16 w; 1: L1 pack; 2: L2 pack; 3: q/s planes */
     const uint16_t *w;
+    const int8_t *q;
+    const uint16_t *s;
     const uint8_t *pack;
     int n, k, group, tsi, cols;
     const uint16_t *x;
@@ -323,27 +331,62 @@ typedef struct {
 
 #define ROW_BATCH 8
 
+/* w = f32(q) * f32(scale), unrounded (main.rs:2289), for one row of a layout. */
+static void row_f32(const gemv_job *j, int row, float *out)
+{
+    int k = j->k;
+    switch (j->kind) {
+    case 1: {
+        int rr;
+        size_t off = l1_tile_off(row, j->n, k, j->group, j->tsi, j->cols, &rr);
+        size_t nibble_bytes = (size_t)j->tsi * k / 2;
+        int gpr = k / j->group;
+        for (int kk = 0; kk < k; kk++) {
+            uint8_t b = j->pack[off + (size_t)rr * (k / 2) + kk / 2];
+            int qv = sext4((kk & 1) ? (b >> 4) : (b & 0x0F));
+            size_t o = off + nibble_bytes + ((size_t)rr * gpr + kk / j->group) * 2;
+            out[kk] = (float)qv * q4o_bf16_to_f32((uint16_t)(j->pack[o] | (j->pack[o + 1] << 8)));
+        }
+        break;
+    }
+    case 2: {
+        int chunks = k / L2_TILE_K;
+        for (int c = 0; c < chunks; c++) {
+            int r;
+            size_t off = l2_block_off(row, c, j->n, k, &r);
+            for (int g = 0; g < 64; g++) {
+                size_t sb = off + 16384 + ((size_t)g * 16 + r) * 2;
+                float sf = q4o_bf16_to_f32((uint16_t)(j->pack[sb] | (j->pack[sb + 1] << 8)));
+                for (int kk = 0; kk < 32; kk++) {
+                    uint8_t b = j->pack[off + (size_t)g * 256 + kk * 8 + r / 2];
+                    unsigned nib = (r % 2 == 0) ? (b & 0x0F) : (b >> 4);
+                    out[c * L2_TILE_K + g * 32 + kk] = (float)sext4(nib) * sf;
+                }
+            }
+        }
+        break;
+    }
+    default: { /* planes */
+        const int8_t *q = j->q + (size_t)row * k;
+        const uint16_t *s = j->s + (size_t)row * (k / 32);
+        for (int kk = 0; kk < k; kk++) out[kk] = (float)q[kk] * q4o_bf16_to_f32(s[kk / 32]);
+    }
+    }
+}
+
 static void gemv_rows(const gemv_job *j)
 {
     int k = j->k;
-    /* scratch for rows dequantized from a pack (kinds 1 and 2) */
-    uint16_t *scratch = NULL;
+    /* scratch for rows of f32 weights (kinds 1-3) */
+    float *scratch = NULL;
     if (j->kind != 0) {
-        scratch = (uint16_t *)malloc((size_t)ROW_BATCH * k * sizeof(uint16_t));
+        scratch = (float *)malloc((size_t)ROW_BATCH * k * sizeof(float));
         if (!scratch) return;
     }
     for (int i0 = j->r0; i0 < j->r1; i0 += ROW_BATCH) {
         int nb = j->r1 - i0 < ROW_BATCH ? j->r1 - i0 : ROW_BATCH;
-        const uint16_t *rows[ROW_BATCH];
-        if (j->kind == 0) {
-            for (int b = 0; b < nb; b++) rows[b] = j->w + (size_t)(i0 + b) * k;
-        } else {
-            if (j->kind == 1)
-                q4o_l1_dequant_rows(j->pack, j->n, k, j->group, j->tsi, j->cols, i0, i0 + nb, scratch);
-            else
-                q4o_l2_dequant_rows(j->pack, j->n, k, i0, i0 + nb, scratch);
-            for (int b = 0; b < nb; b++) rows[b] = scratch + (size_t)b * k;
-        }
+        if (j->kind != 0)
+            for (int b = 0; b < nb; b++) row_f32(j, i0 + b, scratch + (size_t)b * k);
         for (int mm = 0; mm < j->m; mm++) {
             const uint16_t *xm = j->x + (size_t)mm * k;
             float acc[ROW_BATCH] = {0};
@@ -352,7 +395,9 @@ static void gemv_rows(const gemv_job *j)
             for (int kk = 0; kk < k; kk++) {
                 float xv = q4o_bf16_to_f32(xm[kk]);
                 for (int b = 0; b < nb; b++) {
-                    float p = q4o_bf16_to_f32(rows[b][kk]) * xv;
+                    float w = j->kind == 0 ? q4o_bf16_to_f32(j->w[(size_t)(i0 + b) * k + kk])
+                                           : scratch[(size_t)b * k + kk];
+                    float p = w * xv;
                     acc[b] = acc[b] + p;
                 }
             }
@@ -425,6 +470,16 @@ int q4o_gemv_l2(const uint8_t *pack, int n, int k, const uint16_t *x, int m,
     if (m <= 0 || !l2_geom_ok(n, k)) return Q4O_EINVAL;
     gemv_job j = {0};
     j.kind = 2; j.pack = pack; j.n = n; j.k = k; j.x = x; j.m = m; j.y = y;
+    return run_gemv(j, nthreads);
+}
+
+/* Same over q/s planes: q int8 [n][k] in [-8, 7], scale bits [n][k/32]. */
+int q4o_gemv_q(const int8_t *q, const uint16_t *s, int n, int k, const uint16_t *x, int m,
+               float *y, int nthreads)
+{
+    if (m <= 0 || n <= 0 || k <= 0 || k % 32) return Q4O_EINVAL;
+    gemv_job j = {0};
+    j.kind = 3; j.q = q; j.s = s; j.n = n; j.k = k; j.group = 32; j.x = x; j.m = m; j.y = y;
     return run_gemv(j, nthreads);
 }
 

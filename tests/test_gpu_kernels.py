@@ -3,11 +3,17 @@
 Bars (stated per test):
   * dequant: bit-exact RNE_bf16(q * s) for every weight;
   * KAT data (exact arithmetic): bit-exact outputs;
-  * seeded synthetic data: max relative error <= 1e-2 (denominator |ref| +
-    1e-6, crates/xnpu-cli/src/main.rs:2713) and mean absolute error <= 1e-3
-    against the oracle's f32-accumulated result before its final rounding,
-    plus the reference's golden tier |g - w| <= 0.01 + 0.01|w|
-    (main.rs:2705-2714).
+  * seeded synthetic data: max relative error <= 1e-2 and mean absolute error
+    <= 1e-3 against the oracle's output of the same type (the f32-accumulated
+    result itself for f32 outputs, its single RNE to bf16 for bf16 outputs:
+    the reference's own output, main.rs:2287-2296), plus the reference's
+    golden tier |g - w| <= 0.01 + 0.01|w| (main.rs:2705-2714).  The relative
+    error's denominator is max(|ref|, 1e-2 * rms(ref)): any two f32 summation
+    orders of a K-term dot product differ by ~1e-7..1e-6 absolute, which is
+    more than 1e-2 relative for the rare outputs within ~1e-4 of zero (the
+    reference itself only reports |g-w|/(|w|+1e-6), main.rs:2713, and gates
+    on the absolute+relative tier).  The unfloored figure is reported on
+    failure.
 """
 import json
 import struct
@@ -40,18 +46,24 @@ def import_planes(dev, q, s, **kw):
 
 
 def rel_metrics(got, ref):
+    """(max relative error with the floored denominator, mean absolute error,
+    max relative error with the unfloored |ref| + 1e-6 denominator)."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     err = np.abs(got - ref)
-    return float((err / (np.abs(ref) + 1e-6)).max()), float(err.mean())
+    floor = 1e-2 * np.sqrt(np.mean(ref ** 2))
+    return (float((err / np.maximum(np.abs(ref), floor)).max()), float(err.mean()),
+            float((err / (np.abs(ref) + 1e-6)).max()))
 
 
 def assert_parity(y_gpu_bits, y_ref_f32, what):
+    """bf16 GPU output vs the oracle's bf16 output (its f32 sum, one RNE)."""
     got = synth.bf16_bits_to_f32(y_gpu_bits)
-    max_rel, mae = rel_metrics(got, y_ref_f32)
     ref_b = synth.bf16_bits_to_f32(O.round_bf16(y_ref_f32))
+    max_rel, mae, raw = rel_metrics(got, ref_b)
     tier_ok = np.all(np.abs(got - ref_b) <= 0.01 + 0.01 * np.abs(ref_b))
-    assert max_rel <= MAX_REL and mae <= MAE and tier_ok, f"{what}: max_rel={max_rel:.3e} mae={mae:.3e}"
+    assert max_rel <= MAX_REL and mae <= MAE and tier_ok, \
+        f"{what}: max_rel={max_rel:.3e} mae={mae:.3e} (unfloored {raw:.3e})"
 
 
 # ------------------------------------------------------------------ dequant
@@ -143,8 +155,8 @@ def test_gemv_reference_goldens(dev, golden_dir):
 
 # ------------------------------------------------------------------ synthetic parity
 def oracle_rows(q, s, x, rows):
-    w = O.dequant_planes(q[rows], s[rows])
-    return O.gemv_bf16(w, x)
+    """The reference's GEMV (main.rs:2287-2296) on the given rows, f32."""
+    return O.gemv_q(q[rows], s[rows], x)
 
 
 def row_subset(n, limit=1536, seed=0):
@@ -206,7 +218,7 @@ def test_gemv_f32_output(dev):
     w = import_planes(dev, q, s)
     y = hal.linear(w, to_dev_u16(x), out_dtype=torch.float32).cpu().numpy()
     ref = oracle_rows(q, s, x, np.arange(n))
-    max_rel, mae = rel_metrics(y, ref)
+    max_rel, mae, _ = rel_metrics(y, ref)
     assert max_rel <= MAX_REL and mae <= MAE, (max_rel, mae)
     # argmax / top-8 / rel_rms gate of the reference's lm_head check (main.rs:4059-4097)
     assert int(np.argmax(y[0])) == int(np.argmax(ref[0]))
@@ -223,13 +235,35 @@ def test_output_guard_band(dev):
     w = import_planes(dev, q, s)
     x = to_dev_u16(synth.synth_x(m, k, 500))
     pad = 64
-    buf = torch.full((m * n + 2 * pad,), 12345.0, dtype=torch.bfloat16, device="cuda")
+    canary = 12288.0  # exactly representable in bf16
+    buf = torch.full((m * n + 2 * pad,), canary, dtype=torch.bfloat16, device="cuda")
     out = buf[pad:pad + m * n].view(m, n)
     # out must be 16-byte aligned: pad*2 = 128 bytes keeps the allocation's alignment
     hal.linear(w, x, out=out)
     torch.cuda.synchronize()
     b = buf.float().cpu().numpy()
-    assert np.all(b[:pad] == 12345.0) and np.all(b[pad + m * n:] == 12345.0)
+    assert np.all(b[:pad] == canary) and np.all(b[pad + m * n:] == canary)
+    assert not np.any(b[pad:pad + m * n] == canary)
+
+
+def test_stream_order_on_default_stream(dev):
+    """The op is ordered after earlier work on the caller's stream, here the
+    CUDA default stream: a NaN fill queued just before it (no host sync) must
+    be fully overwritten, call after call."""
+    n, k = 4096, 14336
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 450))
+    s = synth.synth_scales(n, k, 450)
+    w = import_planes(dev, q, s)
+    assert torch.cuda.current_stream().cuda_stream == 0  # the default stream
+    for m in (1, 3, 8):
+        x = to_dev_u16(synth.synth_x(m, k, 451 + m))
+        for _ in range(3):
+            filler = torch.randn(2048, 2048, device="cuda") @ torch.randn(2048, 2048, device="cuda")
+            y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+            hal.linear(w, x, out_dtype=torch.float32, out=y)
+            assert not torch.isnan(y).any().item(), m
+            del filler
+    assert dev.fault() == 0
 
 
 # ------------------------------------------------------------------ HAL path
@@ -252,3 +286,4 @@ def test_hal_buffer_op_timeline(dev):
         hal.timeline_wait(dev, seqs[-1] + 5, 1000)  # never submitted
     with pytest.raises(hal.Xq4Error):
         hal.LinearOp(w, xb, yb, m + 1).submit(dev)  # x buffer too small for m=2
+    assert dev.fault() == 0

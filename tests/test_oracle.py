@@ -108,6 +108,23 @@ def test_l2_general_reader_agrees_with_reference_row_reader():
         assert np.array_equal(O.l2_row_ref(pack, m, k, row), w[row])
 
 
+def test_gemv_same_over_every_layout():
+    """The reference's GEMV (w = q*s unrounded, main.rs:2287-2296) gives the
+    same bits over q/s planes, the L1 pack and the L2 pack, and differs from
+    the bf16-weight form only by the weights' rounding."""
+    m, k = 128, 4096
+    q = synth.unpack_codes_signed(synth.synth_codes(m, k, 31))
+    s = synth.synth_scales(m, k, 31)
+    x = synth.synth_x(3, k, 31)
+    yq = O.gemv_q(q, s, x)
+    assert np.array_equal(yq, O.gemv_l1(O.l1_pack(q, s, tsi=16), m, k, 16, x))
+    assert np.array_equal(yq, O.gemv_l2(O.l2_pack(q, s), m, k, x))
+    yb = O.gemv_bf16(O.dequant_planes(q, s), x)
+    assert np.abs(yq - yb).max() < 1e-2 * np.abs(yq).max()
+    # one thread or eight: same bits (rows are independent)
+    assert np.array_equal(yq, O.gemv_q(q, s, x, nthreads=1))
+
+
 def test_l1_dequant_equals_planes():
     m, k = 128, 6144
     q = synth.unpack_codes_signed(synth.synth_codes(m, k, 9))

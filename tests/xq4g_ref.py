@@ -18,12 +18,13 @@ def decode(img, n, k):
     rb = np.arange(nb)[:, None, None]
     ch = np.arange(kc)[None, :, None]
     for j in range(4):
+        G, H = j >> 1, j & 1  # word j: scale group G, half H
         w = words[:, :, :, j]
         for s in range(4):
             for odd in range(2):
                 nib = ((w >> np.uint32(4 * (s + 4 * odd))) & np.uint32(0xF)).astype(np.int16) - 8
                 rows = rb * 16 + (g + 8 * (s & 1))[None, None, :]
-                cols = ch * 64 + (16 * t + 4 * j + 2 * (s >> 1) + odd)[None, None, :]
+                cols = ch * 64 + (32 * G + 8 * t + 4 * H + 2 * (s >> 1) + odd)[None, None, :]
                 q[np.broadcast_to(rows, nib.shape), np.broadcast_to(cols, nib.shape)] = nib
     sc = u[:, :, 512:576].copy().view("<u2").reshape(nb, kc, 8, 2, 2)  # [rb, kc, g, grp, rhi]
     s_full = np.zeros((nb * 16, kc * 2), dtype=np.uint16)

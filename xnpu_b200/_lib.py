@@ -92,6 +92,7 @@ SIGNATURES = {
     "xq4_linear_raw": (_I, [_P, _P, _P, _I, _I, _P]),
     "xq4_wait": (_I, [_P, ctypes.c_uint64, ctypes.c_int64]),
     "xq4_last_seq": (ctypes.c_uint64, [_P]),
+    "xq4_device_fault": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),
     "xq4_comm_unique_id": (_I, [_P]),
     "xq4_comm_init": (_I, [_P, _I, _I, _P, _PP]),
     "xq4_comm_destroy": (_I, [_P]),

@@ -130,6 +130,7 @@ extern "C" void *xq4_device_stream(xq4_device *dev) { return dev ? (void *)dev->
 // ------------------------------------------------------------------ buffers
 struct xq4_buffer {
     xq4_device *dev;
+    int ordinal;  // destroy does not touch `dev`, which may be closed already
     void *ptr;
     size_t bytes;
 };
@@ -147,7 +148,7 @@ extern "C" int xq4_buffer_create(xq4_device *dev, size_t bytes, xq4_buffer **out
         cudaGetLastError();
         return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
     }
-    xq4_buffer *b = new (std::nothrow) xq4_buffer{dev, p, bytes};
+    xq4_buffer *b = new (std::nothrow) xq4_buffer{dev, dev->ordinal, p, bytes};
     if (!b) {
         cudaFree(p);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -193,8 +194,8 @@ extern "C" int xq4_buffer_destroy(xq4_buffer *buf)
 {
     xq4_clear_error();
     if (!buf) return XQ4_OK;
-    cudaSetDevice(buf->dev->ordinal);
-    cudaStreamSynchronize(buf->dev->stream);  // no queued op may still use it
+    cudaSetDevice(buf->ordinal);
+    cudaDeviceSynchronize();  // no queued op may still use it
     cudaError_t e = cudaFree(buf->ptr);
     delete buf;
     if (e != cudaSuccess) return cuda_fail(e, "cudaFree");
@@ -241,6 +242,7 @@ extern "C" int xq4_weight_import(xq4_device *dev, const void *src, size_t src_le
         return xq4_fail(XQ4_ENOMEM, "host allocation");
     }
     w->dev = dev;
+    w->ordinal = dev->ordinal;
     w->n = n;
     w->k = k;
     w->nb = xq4g_nb(n);
@@ -255,8 +257,8 @@ extern "C" int xq4_weight_destroy(xq4_weight *w)
 {
     xq4_clear_error();
     if (!w) return XQ4_OK;
-    cudaSetDevice(w->dev->ordinal);
-    cudaStreamSynchronize(w->dev->stream);
+    cudaSetDevice(w->ordinal);
+    cudaDeviceSynchronize();  // no queued op may still use it
     cudaError_t e = cudaFree(w->d_pack);
     delete w;
     if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
@@ -278,8 +280,9 @@ extern "C" int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream)
     xq4_clear_error();
     if (!w || !out_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
     if ((uintptr_t)out_dev & 15) return xq4_fail(XQ4_EINVAL, "output must be 16-byte aligned");
-    CK(cudaSetDevice(w->dev->ordinal), "cudaSetDevice");
-    cudaStream_t st = stream ? (cudaStream_t)stream : w->dev->stream;
+    CK(cudaSetDevice(w->ordinal), "cudaSetDevice");
+    // NULL is CUDA's default stream, as everywhere in the CUDA API
+    cudaStream_t st = (cudaStream_t)stream;
     CK(xq4_launch_dequant(w->d_pack, w->n, w->k, out_dev, st), "dequant launch");
     return XQ4_OK;
 }
@@ -326,8 +329,10 @@ extern "C" int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_de
 {
     xq4_clear_error();
     if (!w || !x_dev || !y_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
-    cudaStream_t st = stream ? (cudaStream_t)stream : w->dev->stream;
-    return launch_linear(w, x_dev, y_dev, m, out_dtype, st);
+    // NULL is CUDA's default stream (not the device queue): a caller on the
+    // default stream gets its own stream order.
+    CK(cudaSetDevice(w->ordinal), "cudaSetDevice");
+    return launch_linear(w, x_dev, y_dev, m, out_dtype, (cudaStream_t)stream);
 }
 
 static uint64_t now_ns()
@@ -365,3 +370,13 @@ extern "C" int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns)
 }
 
 extern "C" uint64_t xq4_last_seq(const xq4_device *dev) { return dev ? dev->last_seq : 0; }
+
+extern "C" int xq4_device_fault(xq4_device *dev, uint32_t *bits)
+{
+    xq4_clear_error();
+    if (!dev || !bits) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    CK(cudaDeviceSynchronize(), "synchronize before reading the fault word");
+    *bits = xq4_take_fault_gemv() | xq4_take_fault_gemm();
+    return XQ4_OK;
+}

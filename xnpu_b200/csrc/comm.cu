@@ -143,7 +143,7 @@ extern "C" int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w, const voi
     if (!a->ok) return xq4_fail(XQ4_ENCCL, "libnccl.so.2 could not be loaded");
     cudaError_t e = cudaSetDevice(xq4_device_ordinal(comm->dev));
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
-    cudaStream_t st = stream ? (cudaStream_t)stream : xq4_device_cuda_stream(comm->dev);
+    cudaStream_t st = (cudaStream_t)stream;  // NULL = CUDA's default stream
     const int f32 = out_dtype == XQ4_OUT_F32;
     const ncclDataType_t dt = f32 ? ncclFloat32 : ncclBfloat16;
     const size_t slice = (size_t)m * ns;  // elements per rank

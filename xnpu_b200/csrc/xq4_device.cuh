@@ -3,6 +3,17 @@
 #include <stdint.h>
 #include <cuda_runtime.h>
 
+// Set by a kernel whose bounded wait ran out (a pipeline that stopped making
+// progress); the kernel returns instead of spinning forever.  One copy per
+// translation unit (no relocatable device code); each unit that launches
+// kernels with bounded waits exposes a host reader (xq4_take_fault_*), and
+// xq4_device_fault() collects them.
+static __device__ unsigned int g_xq4_fault;
+
+#define XQ4_FAULT_GEMV_FULL 0x1u
+#define XQ4_FAULT_GEMV_EMPTY 0x2u
+#define XQ4_FAULT_GEMM_WAIT 0x4u
+
 namespace xq4d {
 
 // Streamed weight bytes: read once, do not pollute L1.
@@ -67,6 +78,47 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t s_lo, uint32_t
     a[3] = fma_bf16x2(fma_bf16x2(p3, kOne, kNeg136), s_hi, kNegZero);
 }
 
+// Unpack one XQ4G code word into the four bf16x2 mma A-fragment registers
+// holding p = 128 + code = q + 136, exactly (no arithmetic, 7 instructions).
+__device__ __forceinline__ void unpack_word_p(uint32_t w, uint32_t (&a)[4])
+{
+    const uint32_t kMask = 0x000F000Fu, kMagic = 0x43004300u;
+#ifdef XQ4_SHIFT_ON_FMA_PIPE
+    // w >> 4s as the high word of w * 2^(32-4s): an integer multiply, which
+    // leaves the integer ALU pipe to the lop3s
+    a[0] = lop3_and_or(w, kMask, kMagic);
+    a[1] = lop3_and_or(__umulhi(w, 1u << 28), kMask, kMagic);
+    a[2] = lop3_and_or(__umulhi(w, 1u << 24), kMask, kMagic);
+    a[3] = lop3_and_or(__umulhi(w, 1u << 20), kMask, kMagic);
+#else
+    a[0] = lop3_and_or(w, kMask, kMagic);
+    a[1] = lop3_and_or(w >> 4, kMask, kMagic);
+    a[2] = lop3_and_or(w >> 8, kMask, kMagic);
+    a[3] = lop3_and_or(w >> 12, kMask, kMagic);
+#endif
+}
+
+// Unpack one XQ4G code word into the four bf16x2 mma A-fragment registers
+// holding q = code - 8 in [-8, 7], exactly: p = 128 + code, then p - 136.
+__device__ __forceinline__ void unpack_word_q(uint32_t w, uint32_t (&a)[4])
+{
+    const uint32_t kOne = 0x3F803F80u, kNeg136 = 0xC308C308u;
+    unpack_word_p(w, a);
+#pragma unroll
+    for (int i = 0; i < 4; i++) a[i] = fma_bf16x2(a[i], kOne, kNeg136);
+}
+
+// D = A(16x16, row) * B(16x8, col), bf16 in, f32 out (zero accumulator).
+__device__ __forceinline__ void mma_bf16_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    const float z = 0.f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+
 // D += A(16x16, row) * B(16x8, col), bf16 in, f32 accumulate.
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                                uint32_t b1)
@@ -76,6 +128,77 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------ mbarrier / bulk
+__device__ __forceinline__ uint32_t smem_u32(const void *p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make barrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void fence_barrier_init()
+{
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false if the phase did not complete within `limit` polls
+// (each try_wait itself blocks for a hardware-defined interval).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 24))
+{
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// Bulk global -> shared copy (no multicast), completion counted on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Programmatic dependent launch: wait for the preceding grid's memory, and
+// let the next grid start launching.  No-ops without the launch attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void named_bar_sync(int id, int threads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace xq4d

@@ -23,6 +23,7 @@ int xq4_repack_rows(const void *src, size_t src_len, const xq4_layout_desc *desc
 // A weight resident in HBM, in XQ4G layout.
 struct xq4_weight {
     struct xq4_device *dev;
+    int ordinal;       // device ordinal (destroy does not touch `dev`)
     int n, k;          // logical rows / reduction length
     int nb, kc;        // row blocks, 64-K chunks
     uint8_t *d_pack;   // xq4g_bytes(n, k) bytes
@@ -36,6 +37,8 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
 cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);
+unsigned int xq4_take_fault_gemv();
+unsigned int xq4_take_fault_gemm();
 cudaStream_t xq4_device_cuda_stream(struct xq4_device *dev);
 int xq4_device_ordinal(const struct xq4_device *dev);
 #endif

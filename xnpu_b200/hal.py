@@ -88,6 +88,12 @@ class Device:
     def last_seq(self):
         return lib().xq4_last_seq(self.handle)
 
+    def fault(self):
+        """Read and clear the kernels' pipeline-fault bits (0 = none)."""
+        bits = ctypes.c_uint32()
+        check(lib().xq4_device_fault(self.handle, ctypes.byref(bits)))
+        return bits.value
+
     def close(self):
         if self._h is not None:
             h, self._h = self._h, None
