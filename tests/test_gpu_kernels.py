@@ -209,6 +209,29 @@ def test_gemv_parity_ragged(dev, n, k, m):
     assert_parity(y, oracle_rows(q, s, x, np.arange(n)), f"{n}x{k} m={m}")
 
 
+@pytest.mark.parametrize("m,k", [(1, 4096), (3, 4096), (2, 8192), (8, 2048), (4, 14336)])
+def test_gemv_extreme_activation_magnitudes(dev, m, k):
+    """Tokens whose activations span huge, tiny and mixed magnitudes (the
+    fp16-staged decode path rescales each token by a power of two; the bf16
+    path takes x as is)."""
+    n = 512
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 700 + m))
+    s = synth.synth_scales(n, k, 700 + m)
+    rng = np.random.default_rng(701 + m)
+    xf = rng.standard_normal((m, k)).astype(np.float32)
+    mags = [1e30, 1e-30, 1.0, 3e4, 1e-3, 7e10, 2e-20, 1e5][:m]
+    for t in range(m):
+        xf[t] *= mags[t]
+    xf[0, ::97] *= 1e-12  # tiny values mixed into the huge token
+    x = synth.f32_to_bf16_bits(xf)
+    w = import_planes(dev, q, s)
+    y = hal.linear(w, to_dev_u16(x), out_dtype=torch.float32).cpu().numpy()
+    ref = O.gemv_q(q, s, x)
+    for t in range(m):  # per token: each has its own scale
+        max_rel, mae, _ = rel_metrics(y[t], ref[t])
+        assert max_rel <= 1e-3, (t, mags[t], max_rel)
+
+
 def test_gemv_f32_output(dev):
     """lm_head-style f32 logits (no final rounding)."""
     n, k = 4096, 4096

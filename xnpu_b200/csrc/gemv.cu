@@ -10,24 +10,34 @@
 //  * Persistent grid, one CTA per SM.  CTA c owns the contiguous row blocks
 //    [c*nb/G, (c+1)*nb/G); in the XQ4G layout that is ONE contiguous byte
 //    range, streamed front to back.
-//  * A producer thread copies the range into an 8-stage shared-memory ring
-//    with cp.async.bulk (the bulk-copy engine, no multicast); one stage = 32
-//    consecutive 64-K chunks (18 KB) of one row block, completion counted on
-//    a per-stage mbarrier.  147 KB in flight per SM keeps HBM busy (measured
-//    6.2 TB/s for the copy stream alone).
-//  * 16 consumer warps take two chunks each per stage (two independent
-//    instruction streams per warp).  A lane's 16 code bytes
-//    are exactly its mma.m16n8k16 A fragments for the chunk's 4 K steps, and
-//    each K step lies in one 32-K scale group (xq4_layout.h).  The unpack is
-//    one lop3 per bf16x2 pair (p = 128 + code, exact) and one fma.rn.bf16x2
-//    (q = p - 136, exact).  The tensor core forms T = sum q*x over the
-//    group's 32 K (two K steps, f32) and the group adds s * T in f32.  In
-//    exact arithmetic that is sum (q*s)*x, the reference's formula with the
-//    weight never rounded (the rounded RNE_bf16(q*s) is the dequant op's
-//    output, dequant.cu); only the f32 summation order differs.
-//  * The activation slice of a chunk is loaded before the stage wait.
-//  * At the end of a row block the per-warp partials are summed through
-//    shared memory in fixed warp order (deterministic) and written once.
+//  * A producer thread copies the range into a shared-memory ring with
+//    cp.async.bulk (the bulk-copy engine, no multicast): 4 stages of 64
+//    consecutive 64-K chunks (36 KB) of one row block, completion counted on
+//    a per-stage mbarrier.  147 KB in flight per SM keeps HBM busy (the copy
+//    stream alone measured 6.2 TB/s).
+//  * 16 consumer warps take four chunks each per stage (independent
+//    instruction streams per warp; the partial sums accumulate with packed
+//    f32x2 FMAs).  A lane's 16 code bytes are exactly its
+//    mma.m16n8k16 A fragments for the chunk's 4 K steps, and each K step lies
+//    in one 32-K scale group (xq4_layout.h).  The tensor core forms
+//    T = sum q*x over a group's 32 K (two K steps, f32) and the group adds
+//    s * T in f32.  In exact arithmetic that is sum (q*s)*x, the reference's
+//    formula with the weight never rounded (the rounded RNE_bf16(q*s) is the
+//    dequant op's output, dequant.cu); only the f32 summation order differs.
+//  * Unpack, bf16 path: one lop3 per pair (p = 128 + code, bf16 magic) after a
+//    shift of the word by 0/4/8/12, then fma.rn.bf16x2 (q = p - 136, exact).
+//  * Unpack, fp16 path (m <= 8 and m*k <= 16384, i.e. batch-1/few-token
+//    decode): fp16's 10-bit mantissa holds the nibbles at bits 0-3 and 4-7 of
+//    each half under one magic, so a word needs one shift instead of three
+//    (the integer ALU pipe is this kernel's limit).  x is staged once per CTA
+//    in shared memory as fp16 scaled by a per-token power of two chosen from
+//    the token's max |x| (exact for every value within 2^30 of that max;
+//    below it the fp16 rounding error is under 2^-40 of the max), and the
+//    output is scaled back by the inverse power of two (exact).
+//  * At the end of a row block each warp leaves its partial sums in one of
+//    four shared-memory buffers and carries on; one warp (rotating with the
+//    row block) waits for the 16 partials, sums them in fixed warp order
+//    (deterministic) and writes the outputs once.  No all-warp rendezvous.
 //  * Programmatic dependent launch: the producer starts streaming weights
 //    before griddepcontrol.wait; only the consumers (which read x and write
 //    y) wait for the preceding kernel.
@@ -35,6 +45,7 @@
 //    the kernel returns.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "xq4_internal.h"
@@ -43,122 +54,168 @@
 
 namespace {
 
-#ifndef XQ4_GEMV_CPW
-#define XQ4_GEMV_CPW 2
-#endif
 #ifndef XQ4_GEMV_STAGES
-#define XQ4_GEMV_STAGES 8
+#define XQ4_GEMV_STAGES 4
 #endif
 constexpr int kConsumerWarps = 16;
-constexpr int kCpw = XQ4_GEMV_CPW;                    // chunks per consumer warp per stage
-constexpr int kStageChunks = kConsumerWarps * kCpw;
+constexpr int kStageChunks = 64;  // chunks per ring stage (36 KB)
+constexpr int kCpw = kStageChunks / kConsumerWarps;  // chunks per consumer warp per stage
 constexpr int kStages = XQ4_GEMV_STAGES;
+#ifndef XQ4_GEMV_CTAS_PER_SM
+#define XQ4_GEMV_CTAS_PER_SM 1
+#endif
+constexpr int kCtasPerSm = XQ4_GEMV_CTAS_PER_SM;  // resident CTAs per SM (grid = SMs x this)
 constexpr int kStageBytes = kStageChunks * XQ4G_UNIT_BYTES;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kBarBytes = ((2 * kStages + 2) * 8 + 127) & ~127;  // full/empty/reduce mbarriers, padded
-static_assert(kBarBytes >= (2 * kStages + 2) * 8, "barrier region too small");
+constexpr int kRedBufs = 4;  // row-block partial buffers in flight
+constexpr int kBarBytes = ((2 * kStages + 2 * kRedBufs) * 8 + 127) & ~127;  // ring + reduce mbarriers, padded
+static_assert(kBarBytes >= (2 * kStages + 2 * kRedBufs) * 8, "barrier region too small");
 constexpr int kMaxSmem = 227 * 1024;
+#ifndef XQ4_GEMV_XH_MAX
+#define XQ4_GEMV_XH_MAX 16384
+#endif
+constexpr int kXhMaxElems = XQ4_GEMV_XH_MAX;  // fp16 path: m * k_padded must fit this
 
-// Shared-memory plan: [barriers | partials x2 | ring]
-template <int NT>
-__host__ __device__ constexpr size_t red_bytes() { return 2 * (size_t)kConsumerWarps * NT * 128 * 4; }
-template <int NT>
-__host__ __device__ constexpr size_t ring_offset() { return (kBarBytes + red_bytes<NT>() + 127) & ~(size_t)127; }
-template <int NT>
-__host__ __device__ constexpr size_t smem_bytes() { return ring_offset<NT>() + (size_t)kStages * kStageBytes; }
+// Shared-memory plan: [barriers | partials x2 | token exponents | fp16 x | ring]
+__host__ __device__ constexpr size_t xh_offset(int nt) { return kBarBytes + (size_t)kRedBufs * kConsumerWarps * nt * 128 * 4; }
+__host__ __device__ inline size_t ring_offset(int nt, bool xh, int m, int kc_n)
+{
+    size_t o = xh_offset(nt);
+    if (xh) o += 64 + (size_t)m * kc_n * XQ4G_KCHUNK * 2;  // 8 token exponents (+pad), fp16 x
+    return (o + 127) & ~(size_t)127;
+}
+__host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
+{
+    return ring_offset(nt, xh, m, kc_n) + (size_t)kStages * kStageBytes;
+}
 
 // One ring stage for one consumer warp: its chunks kc0 + warp + c*16.  The
 // activation runs are loaded before the stage wait so their latency overlaps
-// it.  SAFE handles a partial stage (chunks past kc_n) and a K tail that is
-// not a whole chunk (k % 64 == 32); the fast path has no per-chunk tests.
-template <int NT, bool SAFE>
+// it.  SAFE handles a partial stage (chunks past kc_n) and, on the bf16 path,
+// a K tail that is not a whole chunk (k % 64 == 32); the fast path has no
+// per-chunk tests.  On the fp16 path xr points at the token's fp16 row in
+// shared memory (zero padded to whole chunks).
+template <int NT, bool SAFE, bool XH>
 __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *full, uint32_t phase, int kc0,
                                               int kc_n, int k, const uint16_t *const (&xr)[NT], int warp,
                                               int lane, float (&acc)[NT][4])
 {
+    // chunks whose activation runs are held in registers at once (bounds
+    // the register file for 16-token tiles)
+    constexpr int R = NT == 1 ? kCpw : 2;
     const int g = lane >> 2, t = lane & 3;
-    uint4 xf[kCpw][NT][2];  // 8 K of group 0 and 8 K of group 1, per chunk
 #pragma unroll
-    for (int c = 0; c < kCpw; c++) {
-        const int kc = kc0 + warp + c * kConsumerWarps;
+    for (int c0 = 0; c0 < kCpw; c0 += R) {
+        uint4 xf[R][NT][2];  // 8 K of group 0 and 8 K of group 1, per chunk
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++)
+        for (int c = 0; c < R; c++) {
+            const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int G2 = 0; G2 < 2; G2++) {
+                    const int kb = kc * XQ4G_KCHUNK + 32 * G2 + 8 * t;
+                    if (XH) {
+                        xf[c][nt][G2] = (!SAFE || kc < kc_n) ? *reinterpret_cast<const uint4 *>(xr[nt] + kb)
+                                                             : make_uint4(0, 0, 0, 0);
+                    } else if (!SAFE || (kc < kc_n && kb < k)) {
+                        xf[c][nt][G2] = xq4d::ldg_v4(xr[nt] + kb);
+                    } else {
+                        xf[c][nt][G2] = make_uint4(0, 0, 0, 0);
+                    }
+                }
+        }
+        if (c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
+        uint4 cw[R];
+        uint2 sw[R];
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const int cl = warp + (c0 + c) * kConsumerWarps;  // chunk within the stage
+            const uint8_t *up = stage + cl * XQ4G_UNIT_BYTES;
+            if (!SAFE || kc0 + cl < kc_n) {
+                cw[c] = *reinterpret_cast<const uint4 *>(up + lane * 16);
+                sw[c] = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+            } else {
+                cw[c] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
+                sw[c] = make_uint2(0, 0);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const uint32_t words[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
 #pragma unroll
             for (int G2 = 0; G2 < 2; G2++) {
-                const int kb = kc * XQ4G_KCHUNK + 32 * G2 + 8 * t;
-                if (!SAFE || (kc < kc_n && kb < k))
-                    xf[c][nt][G2] = xq4d::ldg_v4(xr[nt] + kb);
-                else
-                    xf[c][nt][G2] = make_uint4(0, 0, 0, 0);
-            }
-    }
-    if (!xq4d::mbar_wait(full, phase)) return false;
-    uint4 cw[kCpw];
-    uint2 sw[kCpw];
+                const uint32_t sg = G2 ? sw[c].y : sw[c].x;
+                const float s_lo = __uint_as_float(sg << 16);    // row g
+                float s_hi = __uint_as_float(sg & 0xFFFF0000u);  // row g+8
+                uint32_t a0[4], a1[4];
+                if (XH) {
+                    s_hi *= 0.0625f;  // rows g+8 carry 16*q (unpack_word_h16)
+                    xq4d::unpack_word_h16(words[2 * G2], a0);
+                    xq4d::unpack_word_h16(words[2 * G2 + 1], a1);
+                } else {
+                    xq4d::unpack_word_q(words[2 * G2], a0);
+                    xq4d::unpack_word_q(words[2 * G2 + 1], a1);
+                }
 #pragma unroll
-    for (int c = 0; c < kCpw; c++) {
-        const int cl = warp + c * kConsumerWarps;  // chunk within the stage
-        const uint8_t *up = stage + cl * XQ4G_UNIT_BYTES;
-        if (!SAFE || kc0 + cl < kc_n) {
-            cw[c] = *reinterpret_cast<const uint4 *>(up + lane * 16);
-            sw[c] = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
-        } else {
-            cw[c] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
-            sw[c] = make_uint2(0, 0);
-        }
-    }
-#pragma unroll
-    for (int c = 0; c < kCpw; c++) {
-        const uint32_t words[4] = {cw[c].x, cw[c].y, cw[c].z, cw[c].w};
-#pragma unroll
-        for (int G2 = 0; G2 < 2; G2++) {
-            const uint32_t sg = G2 ? sw[c].y : sw[c].x;
-            const float s_lo = __uint_as_float(sg << 16);          // row g
-            const float s_hi = __uint_as_float(sg & 0xFFFF0000u);  // row g+8
-            uint32_t a0[4], a1[4];
-            xq4d::unpack_word_q(words[2 * G2], a0);
-            xq4d::unpack_word_q(words[2 * G2 + 1], a1);
-#pragma unroll
-            for (int nt = 0; nt < NT; nt++) {
-                float tacc[4];
-                xq4d::mma_bf16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
-                xq4d::mma_bf16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
-                acc[nt][0] = fmaf(s_lo, tacc[0], acc[nt][0]);
-                acc[nt][1] = fmaf(s_lo, tacc[1], acc[nt][1]);
-                acc[nt][2] = fmaf(s_hi, tacc[2], acc[nt][2]);
-                acc[nt][3] = fmaf(s_hi, tacc[3], acc[nt][3]);
+                for (int nt = 0; nt < NT; nt++) {
+                    float tacc[4];
+                    if (XH) {
+                        xq4d::mma_f16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
+                        xq4d::mma_f16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
+                    } else {
+                        xq4d::mma_bf16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
+                        xq4d::mma_bf16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
+                    }
+                    xq4d::ffma2(acc[nt][0], acc[nt][1], s_lo, tacc[0], tacc[1]);
+                    xq4d::ffma2(acc[nt][2], acc[nt][3], s_hi, tacc[2], tacc[3]);
+                }
             }
         }
     }
     return true;
 }
 
-template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+// 2^e as a product of two normal floats (e in [-252, 254]).
+__device__ __forceinline__ void pow2_split(int e, float &f1, float &f2)
+{
+    const int e1 = e / 2, e2 = e - e1;
+    f1 = __int_as_float((e1 + 127) << 23);
+    f2 = __int_as_float((e2 + 127) << 23);
+}
+
+template <int NT, bool XH>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             const uint16_t *__restrict__ x, int m, void *__restrict__ y, int out_f32)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kStages;
-    uint64_t *red_full = empty + kStages;  // [2], one per partial buffer
+    uint64_t *red_full = empty + kStages;     // [kRedBufs]: all 16 partials written
+    uint64_t *red_free = red_full + kRedBufs;  // [kRedBufs]: reduction done, buffer reusable
     float *red = reinterpret_cast<float *>(smem + kBarBytes);
-    uint8_t *ring = smem + ring_offset<NT>();
+    int *tok_exp = reinterpret_cast<int *>(smem + xh_offset(NT));            // fp16 path: [8]
+    uint16_t *xh = reinterpret_cast<uint16_t *>(smem + xh_offset(NT) + 64);  // fp16 path: [m][kp]
+    uint8_t *ring = smem + ring_offset(NT, XH, m, kc_n);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int rb0 = (int)((long long)cta * nb / G), rb1 = (int)((long long)(cta + 1) * nb / G);
     const int spr = (kc_n + kStageChunks - 1) / kStageChunks;  // stages per row block
     const int total = (rb1 - rb0) * spr;
+    const int kp = kc_n * XQ4G_KCHUNK;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             xq4d::mbar_init(&full[s], 1);
             xq4d::mbar_init(&empty[s], kConsumerWarps);
         }
-        xq4d::mbar_init(&red_full[0], kConsumerWarps);
-        xq4d::mbar_init(&red_full[1], kConsumerWarps);
+        for (int b = 0; b < kRedBufs; b++) {
+            xq4d::mbar_init(&red_full[b], kConsumerWarps);
+            xq4d::mbar_init(&red_free[b], 1);
+        }
         xq4d::fence_barrier_init();
     }
     __syncthreads();
@@ -195,6 +252,57 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     // ------------------------------------------------------------ consumers
     xq4d::grid_dep_wait();  // x is written, y may be read, by the neighbouring kernels
 
+    if (XH) {
+        // Stage x as fp16 with a per-token power of two: max|x| * 2^e lies in
+        // [2^14, 2^15).  Every consumer thread takes 8-element runs (16 bytes);
+        // k is a multiple of 32, so runs never straddle a token.
+        const int runs = k / 8, kp_runs = kp / 8;
+        unsigned *tok_max = reinterpret_cast<unsigned *>(tok_exp);
+        if (threadIdx.x < 8) tok_max[threadIdx.x] = 0;
+        xq4d::named_bar_sync(1, kConsumerThreads);
+        for (int tok = 0; tok < m; tok++) {
+            unsigned mx = 0;  // max |x| as bf16 magnitude bits (ordered like the values)
+            for (int r = threadIdx.x; r < runs; r += kConsumerThreads) {
+                const uint4 v = xq4d::ldg_v4(x + (size_t)tok * k + 8 * r);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) mx = max(mx, max(w[h] & 0x7FFFu, (w[h] >> 16) & 0x7FFFu));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) atomicMax(&tok_max[tok], mx);
+        }
+        xq4d::named_bar_sync(1, kConsumerThreads);
+        if (threadIdx.x < m) {
+            const unsigned mx = tok_max[threadIdx.x];
+            const int ex = (int)(mx >> 7) - 127;  // exponent of the max (bf16 bits)
+            tok_exp[threadIdx.x] = mx == 0 ? 0 : min(max(14 - ex, -252), 254);
+        }
+        xq4d::named_bar_sync(1, kConsumerThreads);
+        for (int tok = 0; tok < m; tok++) {
+            float f1, f2;
+            pow2_split(tok_exp[tok], f1, f2);
+            for (int r = threadIdx.x; r < kp_runs; r += kConsumerThreads) {
+                uint4 o = make_uint4(0, 0, 0, 0);
+                if (r < runs) {
+                    const uint4 v = xq4d::ldg_v4(x + (size_t)tok * k + 8 * r);
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                    uint32_t h2[4];
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const float lo = __uint_as_float(w[h] << 16) * f1 * f2;
+                        const float hi = __uint_as_float(w[h] & 0xFFFF0000u) * f1 * f2;
+                        const __half2 p = __floats2half2_rn(lo, hi);
+                        h2[h] = *reinterpret_cast<const uint32_t *>(&p);
+                    }
+                    o = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+                }
+                *reinterpret_cast<uint4 *>(xh + (size_t)tok * kp + 8 * r) = o;
+            }
+        }
+        xq4d::named_bar_sync(1, kConsumerThreads);
+    }
+
     const int g = lane >> 2, t = lane & 3;
     // B column g of the mma is token g (+8*nt).  A column past m only feeds
     // output columns that are never written, so those lanes read token 0's
@@ -203,7 +311,7 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int tok = g + 8 * nt;
-        xr[nt] = x + (size_t)(tok < m ? tok : 0) * k;
+        xr[nt] = XH ? xh + (size_t)(tok < m ? tok : 0) * kp : x + (size_t)(tok < m ? tok : 0) * k;
     }
     float acc[NT][4];
 #pragma unroll
@@ -216,9 +324,9 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     const bool k_whole = (k % XQ4G_KCHUNK) == 0;
     for (int i = 0; i < total; i++) {
         const uint8_t *stage = ring + (size_t)slot * kStageBytes;
-        const bool ok = (k_whole && kc0 + kStageChunks <= kc_n)
-                            ? consume_stage<NT, false>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc)
-                            : consume_stage<NT, true>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc);
+        const bool fast = (XH || k_whole) && kc0 + kStageChunks <= kc_n;
+        const bool ok = fast ? consume_stage<NT, false, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc)
+                             : consume_stage<NT, true, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc);
         if (!ok) {
             atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
             return;
@@ -232,37 +340,55 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
         kc0 += kStageChunks;
 
         if (kc0 >= kc_n) {  // ------------------------------ row block complete
+            // Every warp leaves its partial in buffer rbl % kRedBufs and moves
+            // on; warp rbl % 16 waits for all 16 partials, sums them in warp
+            // order (deterministic) and writes the row block.  A warp waits
+            // only before reusing a buffer whose reduction is still running.
             kc0 = 0;
-            const int buf = rbl & 1;
-            float *rd = red + (size_t)buf * kConsumerWarps * NT * 128;
+            const int buf = rbl % kRedBufs;
+            const uint32_t use = (uint32_t)(rbl / kRedBufs);
+            if (use > 0 && !xq4d::mbar_wait(&red_free[buf], (use - 1) & 1)) {
+                atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                return;
+            }
+            float *rd = red + (size_t)buf * kConsumerWarps * NT * 128;  // [warp][tok][row]
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                float *r = rd + ((size_t)warp * NT + nt) * 128;
-                r[g * 8 + 2 * t] = acc[nt][0];
-                r[g * 8 + 2 * t + 1] = acc[nt][1];
-                r[(g + 8) * 8 + 2 * t] = acc[nt][2];
-                r[(g + 8) * 8 + 2 * t + 1] = acc[nt][3];
+                float *r = rd + (size_t)warp * NT * 128 + (size_t)nt * 128;
+                r[(2 * t) * 16 + g] = acc[nt][0];
+                r[(2 * t + 1) * 16 + g] = acc[nt][1];
+                r[(2 * t) * 16 + g + 8] = acc[nt][2];
+                r[(2 * t + 1) * 16 + g + 8] = acc[nt][3];
                 acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
             }
             __syncwarp();
             if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);
-            if (!xq4d::mbar_wait(&red_full[buf], (uint32_t)(rbl >> 1) & 1)) {
-                atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
-                return;
-            }
-            const int rb = rb0 + rbl;
-            for (int idx = threadIdx.x; idx < NT * 128; idx += kConsumerThreads) {
-                const int nt = idx >> 7, tl = (idx & 127) >> 4, r = idx & 15;
-                float s = 0.f;
-#pragma unroll
-                for (int w = 0; w < kConsumerWarps; w++) s += rd[((size_t)w * NT + nt) * 128 + r * 8 + tl];
-                const int tok = nt * 8 + tl, row = rb * XQ4G_ROWS + r;
-                if (tok < m && row < n) {
-                    if (out_f32)
-                        reinterpret_cast<float *>(y)[(size_t)tok * n + row] = s;
-                    else
-                        reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + row] = __float2bfloat16_rn(s);
+            if (warp == rbl % kConsumerWarps) {  // this row block's reducer
+                if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
+                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                    return;
                 }
+                const int rb = rb0 + rbl;
+                for (int o = lane; o < m * 16; o += 32) {  // o = tok * 16 + row
+                    const int tok = o >> 4, r = o & 15;
+                    float s = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kConsumerWarps; w++) s += rd[(size_t)w * NT * 128 + o];
+                    const int row = rb * XQ4G_ROWS + r;
+                    if (row < n) {
+                        if (XH) {  // undo the token's power of two (exact)
+                            float f1, f2;
+                            pow2_split(-tok_exp[tok], f1, f2);
+                            s = s * f1 * f2;
+                        }
+                        if (out_f32)
+                            reinterpret_cast<float *>(y)[(size_t)tok * n + row] = s;
+                        else
+                            reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + row] = __float2bfloat16_rn(s);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
             }
             rbl++;
         }
@@ -283,7 +409,7 @@ int sm_count_of_current_device()
     return cache[dev];
 }
 
-template <int NT>
+template <int NT, bool XH>
 cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int m, void *y, int out_f32,
                        cudaStream_t st)
 {
@@ -291,16 +417,15 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem_bytes<NT>());
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, XH>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
     const int nb = xq4g_nb(n), kc = xq4g_kc(k);
-    const size_t smem = smem_bytes<NT>();
-    static_assert(smem_bytes<2>() <= (size_t)kMaxSmem, "shared memory plan too large");
+    const size_t smem = smem_bytes(NT, XH, m, kc);
+    if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;  // never for the paths chosen below
     const int sms = sm_count_of_current_device();
-    const int grid = nb < sms ? nb : sms;
+    const int grid = nb < sms * kCtasPerSm ? nb : sms * kCtasPerSm;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -315,7 +440,7 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
 #else
     cfg.numAttrs = 1;
 #endif
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT>, pack, n, k, nb, kc, x, m, y, out_f32);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, XH>, pack, n, k, nb, kc, x, m, y, out_f32);
 }
 
 }  // namespace
@@ -324,15 +449,23 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st)
 {
+    static_assert(xh_offset(2) + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem, "bf16 plan too large");
+    static_assert(xh_offset(1) + 64 + 2 * (size_t)kXhMaxElems + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem,
+                  "fp16 plan too large");
     const size_t ysz = out_f32 ? 4 : 2;
+    const int kp = xq4g_kc(k) * XQ4G_KCHUNK;
+    const uint8_t *p = reinterpret_cast<const uint8_t *>(pack);
     for (int t0 = 0; t0 < m; t0 += 16) {
         const int mt = m - t0 < 16 ? m - t0 : 16;
         const uint16_t *xs = reinterpret_cast<const uint16_t *>(x) + (size_t)t0 * k;
         void *ys = reinterpret_cast<char *>(y) + (size_t)t0 * n * ysz;
-        cudaError_t e = mt <= 8 ? launch_one<1>(reinterpret_cast<const uint8_t *>(pack), n, k, xs, mt, ys,
-                                                out_f32, st)
-                                : launch_one<2>(reinterpret_cast<const uint8_t *>(pack), n, k, xs, mt, ys,
-                                                out_f32, st);
+        cudaError_t e;
+        if (mt <= 8 && (size_t)mt * kp <= (size_t)kXhMaxElems)
+            e = launch_one<1, true>(p, n, k, xs, mt, ys, out_f32, st);
+        else if (mt <= 8)
+            e = launch_one<1, false>(p, n, k, xs, mt, ys, out_f32, st);
+        else
+            e = launch_one<2, false>(p, n, k, xs, mt, ys, out_f32, st);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -108,6 +108,54 @@ __device__ __forceinline__ void unpack_word_q(uint32_t w, uint32_t (&a)[4])
     for (int i = 0; i < 4; i++) a[i] = fma_bf16x2(a[i], kOne, kNeg136);
 }
 
+// d = RNE_f16x2(a * b + c), one rounding.
+__device__ __forceinline__ uint32_t fma_f16x2(uint32_t a, uint32_t b, uint32_t c)
+{
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Unpack one XQ4G code word into the four f16x2 mma A-fragment registers.
+// fp16 has 10 mantissa bits, so the nibbles at bits 0-3 and 4-7 of each half
+// both sit inside the mantissa under the 1024 magic exponent:
+//   (w & 0x000F000F) | 0x6400 -> 1024 + c        - 1032 -> q      (rows g)
+//   (w & 0x00F000F0) | 0x6400 -> 1024 + 16c      - 1152 -> 16 q   (rows g+8)
+// and the same on w >> 8 for nibbles 2/3.  One shift per word instead of
+// three; every value is exact.  Registers 1 and 3 (rows g+8 of the fragment)
+// carry the factor 16, which the caller folds into those rows' scale.
+__device__ __forceinline__ void unpack_word_h16(uint32_t w, uint32_t (&a)[4])
+{
+    const uint32_t kMagic = 0x64006400u, kOne = 0x3C003C00u;
+    const uint32_t kNeg1032 = 0xE408E408u, kNeg1152 = 0xE480E480u;
+    const uint32_t w8 = w >> 8;
+    a[0] = fma_f16x2(lop3_and_or(w, 0x000F000Fu, kMagic), kOne, kNeg1032);
+    a[1] = fma_f16x2(lop3_and_or(w, 0x00F000F0u, kMagic), kOne, kNeg1152);
+    a[2] = fma_f16x2(lop3_and_or(w8, 0x000F000Fu, kMagic), kOne, kNeg1032);
+    a[3] = fma_f16x2(lop3_and_or(w8, 0x00F000F0u, kMagic), kOne, kNeg1152);
+}
+
+// D = A(16x16, row) * B(16x8, col), f16 in, f32 out (zero accumulator).
+__device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    const float z = 0.f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+
+// D += A(16x16, row) * B(16x8, col), f16 in, f32 accumulate.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // D = A(16x16, row) * B(16x8, col), bf16 in, f32 out (zero accumulator).
 __device__ __forceinline__ void mma_bf16_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
@@ -128,6 +176,20 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
         "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (d0, d1) += s * (x0, x1) as one packed f32x2 FMA (sm_100): two independent
+// single-rounding FMAs in one issue slot.
+__device__ __forceinline__ void ffma2(float &d0, float &d1, float s, float x0, float x1)
+{
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %2};\n\t"
+        "mov.b64 rb, {%3, %4};\n\t"
+        "mov.b64 rd, {%0, %1};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(s), "f"(x0), "f"(x1));
 }
 
 // ------------------------------------------------------------ mbarrier / bulk
