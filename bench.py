@@ -54,57 +54,49 @@ def measured_peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons polled through NVML from a
+    host thread every ~2 ms while the timed region runs (read-only queries)."""
+
+    REASONS = {  # NVML clocks-event reason bits
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4,
+    }
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"xq4_clocks_{os.getpid()}.csv"
+        self.rows = []
+        self.err = None
+        self._stop = threading.Event()
+
+    def _poll(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((mhz, bits))
+                time.sleep(0.002)
+        except Exception as e:  # NVML missing: report it, do not fail the bench
+            self.err = f"{type(e).__name__}: {e}"
 
     def __enter__(self):
-        try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.fh, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        self._t = threading.Thread(target=self._poll, daemon=True)
+        self._t.start()
+        time.sleep(0.01)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.fh.close()
+        self._stop.set()
+        self._t.join(timeout=5)
 
     def summary(self):
-        if self.proc is None or not self.path.exists():
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 7:
-                try:
-                    rows.append((float(parts[0]), float(parts[1]), parts[3:7]))
-                except ValueError:
-                    pass
-        try:
-            self.path.unlink()
-        except OSError:
-            pass
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
-        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        reasons = sorted({n for _, b in self.rows for n, bit in self.REASONS.items() if b & bit})
+        return {"sm_mhz": float(np.median([r[0] for r in self.rows])), "sm_max_mhz": float(self.max_mhz),
+                "reasons": reasons, "samples": len(self.rows), "source": "NVML, 2 ms polling"}
 
 
 # ---------------------------------------------------------------- CPU baseline

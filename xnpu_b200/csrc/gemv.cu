@@ -7,15 +7,16 @@
 // at main.rs:2171-2448, :3288-3898).
 //
 // Design (HBM-bound: 0.5625 B of weights per weight, 2*m flops per weight):
-//  * Persistent grid, one CTA per SM.  CTA c owns the contiguous row blocks
+//  * Persistent grid, two CTAs per SM.  CTA c owns the contiguous row blocks
 //    [c*nb/G, (c+1)*nb/G); in the XQ4G layout that is ONE contiguous byte
-//    range, streamed front to back.
+//    range, streamed front to back.  Two independent CTAs per SM (rather than
+//    one twice as large) let the next kernel's CTA move into an SM as soon as
+//    one of them finishes.
 //  * A producer thread copies the range into a shared-memory ring with
-//    cp.async.bulk (the bulk-copy engine, no multicast): 4 stages of 64
-//    consecutive 64-K chunks (36 KB) of one row block, completion counted on
-//    a per-stage mbarrier.  147 KB in flight per SM keeps HBM busy (the copy
-//    stream alone measured 6.2 TB/s).
-//  * 16 consumer warps take four chunks each per stage (independent
+//    cp.async.bulk (the bulk-copy engine, no multicast): 3 stages of 32
+//    consecutive 64-K chunks (18 KB) of one row block, completion counted on
+//    a per-stage mbarrier; 110 KB in flight per SM.
+//  * 8 consumer warps take four chunks each per stage (independent
 //    instruction streams per warp; the partial sums accumulate with packed
 //    f32x2 FMAs).  A lane's 16 code bytes are exactly its
 //    mma.m16n8k16 A fragments for the chunk's 4 K steps, and each K step lies
@@ -36,7 +37,7 @@
 //    output is scaled back by the inverse power of two (exact).
 //  * At the end of a row block each warp leaves its partial sums in one of
 //    four shared-memory buffers and carries on; one warp (rotating with the
-//    row block) waits for the 16 partials, sums them in fixed warp order
+//    row block) waits for the 8 partials, sums them in fixed warp order
 //    (deterministic) and writes the outputs once.  No all-warp rendezvous.
 //  * Programmatic dependent launch: the producer starts streaming weights
 //    before griddepcontrol.wait; only the consumers (which read x and write
@@ -54,15 +55,23 @@
 
 namespace {
 
+// Tuning (measured on B200, see the header): 2 CTAs per SM, each with 8
+// consumer warps and a 3-stage ring of 32-chunk (18 KB) stages.
 #ifndef XQ4_GEMV_STAGES
-#define XQ4_GEMV_STAGES 4
+#define XQ4_GEMV_STAGES 3
 #endif
-constexpr int kConsumerWarps = 16;
-constexpr int kStageChunks = 64;  // chunks per ring stage (36 KB)
+#ifndef XQ4_GEMV_WARPS
+#define XQ4_GEMV_WARPS 8
+#endif
+#ifndef XQ4_GEMV_STAGE_CHUNKS
+#define XQ4_GEMV_STAGE_CHUNKS 32
+#endif
+constexpr int kConsumerWarps = XQ4_GEMV_WARPS;
+constexpr int kStageChunks = XQ4_GEMV_STAGE_CHUNKS;  // chunks per ring stage (576 B each)
 constexpr int kCpw = kStageChunks / kConsumerWarps;  // chunks per consumer warp per stage
 constexpr int kStages = XQ4_GEMV_STAGES;
 #ifndef XQ4_GEMV_CTAS_PER_SM
-#define XQ4_GEMV_CTAS_PER_SM 1
+#define XQ4_GEMV_CTAS_PER_SM 2
 #endif
 constexpr int kCtasPerSm = XQ4_GEMV_CTAS_PER_SM;  // resident CTAs per SM (grid = SMs x this)
 constexpr int kStageBytes = kStageChunks * XQ4G_UNIT_BYTES;
