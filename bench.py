@@ -199,7 +199,14 @@ def main():
                     help="layers of the weight set (32 = the benchmark; fewer only for profiler captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiler captures only")
     ap.add_argument("--skip-lmhead", action="store_true", help="profiler captures only")
+    ap.add_argument("--kernel-case", choices=["gemv", "gemm"],
+                    help="profiler captures: one projection launched warmup+steps times on GPU 0 "
+                         "(gemv: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048)")
+    ap.add_argument("--case-m", type=int, default=None, help="token count of --kernel-case")
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args)
+        return
     global LAYERS
     LAYERS = args.layers
 
@@ -476,6 +483,38 @@ def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
     shard_bytes = algo_bytes(r1 - r0, k, out_bytes=4)
     return {"us": ms * 1e3, "shard_rows": r1 - r0, "gbs_per_gpu": shard_bytes / (ms * 1e-3) / 1e9,
             "logits_allgather_bytes": n * 4 if world > 1 else 0}
+
+
+def kernel_case(args):
+    """One projection launched warmup+steps times through the C ABI (the
+    small, single-kernel command that profiler captures run on)."""
+    import torch
+    from xnpu_b200 import hal, lib, synth
+    from xnpu_b200._lib import check
+    n, k, m = (65536, 4096, 1) if args.kernel_case == "gemv" else (14336, 4096, 2048)
+    m = args.case_m or m
+    dev = hal.Device.open(0)
+    L = lib()
+    w = hal.Weight.import_(dev, synth.planes_bytes(synth.synth_codes(n, k, 31), synth.synth_scales(n, k, 31)),
+                           hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k))
+    x = torch.from_numpy(synth.synth_x(m, k, 32).view(np.int16)).cuda().view(torch.bfloat16)
+    y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.Stream()
+    for _ in range(args.warmup):
+        check(L.xq4_linear_raw(w.handle, x.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        check(L.xq4_linear_raw(w.handle, x.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
+    b.record(stream)
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / max(1, args.steps)
+    print(json.dumps({"kernel_case": args.kernel_case, "n": n, "k": k, "m": m, "us_per_launch": us,
+                      "algo_gbs": algo_bytes(n, k, m) / us / 1e3, "tflops": 2.0 * m * n * k / us / 1e6}),
+          flush=True)
+    w.destroy()
+    dev.close()
 
 
 if __name__ == "__main__":

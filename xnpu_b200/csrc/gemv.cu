@@ -36,9 +36,11 @@
 //    below it the fp16 rounding error is under 2^-40 of the max), and the
 //    output is scaled back by the inverse power of two (exact).
 //  * At the end of a row block each warp leaves its partial sums in one of
-//    four shared-memory buffers and carries on; one warp (rotating with the
-//    row block) waits for the 8 partials, sums them in fixed warp order
-//    (deterministic) and writes the outputs once.  No all-warp rendezvous.
+//    three shared-memory buffers and carries on; a dedicated reducer warp
+//    waits for the 8 partials, sums them in fixed warp order (deterministic)
+//    and writes the outputs once.  No consumer warp ever waits for another
+//    (measured: a rotating reducer among the consumers cost 16% of the
+//    compute time).
 //  * Programmatic dependent launch: the producer starts streaming weights
 //    before griddepcontrol.wait; only the consumers (which read x and write
 //    y) wait for the preceding kernel.
@@ -76,22 +78,33 @@ constexpr int kStages = XQ4_GEMV_STAGES;
 constexpr int kCtasPerSm = XQ4_GEMV_CTAS_PER_SM;  // resident CTAs per SM (grid = SMs x this)
 constexpr int kStageBytes = kStageChunks * XQ4G_UNIT_BYTES;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kRedBufs = 4;  // row-block partial buffers in flight
+constexpr int kProducerWarp = kConsumerWarps;     // one thread issues the bulk copies
+constexpr int kReducerWarp = kConsumerWarps + 1;  // sums the row blocks' partials, writes y
+constexpr int kThreads = kConsumerThreads + 64;
+constexpr int kRedBufs = 3;  // row-block partial buffers in flight
 constexpr int kBarBytes = ((2 * kStages + 2 * kRedBufs) * 8 + 127) & ~127;  // ring + reduce mbarriers, padded
 static_assert(kBarBytes >= (2 * kStages + 2 * kRedBufs) * 8, "barrier region too small");
 constexpr int kMaxSmem = 227 * 1024;
-#ifndef XQ4_GEMV_XH_MAX
-#define XQ4_GEMV_XH_MAX 16384
-#endif
-constexpr int kXhMaxElems = XQ4_GEMV_XH_MAX;  // fp16 path: m * k_padded must fit this
+// fp16 path limits: m * k_padded activations staged per CTA, and the staged
+// x plus the correction table (k_padded * (2m + 1) bytes) small enough that
+// two CTAs still fit on an SM.
+constexpr int kXhMaxElems = 20480;
+constexpr int kXhMaxBytes = 46080;
+__host__ __device__ constexpr bool xh_fits(int m, int kp)
+{
+    return m <= 8 && m * kp <= kXhMaxElems && kp * (2 * m + 1) <= kXhMaxBytes;
+}
 
-// Shared-memory plan: [barriers | partials x2 | token exponents | fp16 x | ring]
+// Shared-memory plan: [barriers | partials | token maxima | fp16 x | correction table | ring]
 __host__ __device__ constexpr size_t xh_offset(int nt) { return kBarBytes + (size_t)kRedBufs * kConsumerWarps * nt * 128 * 4; }
+__host__ __device__ inline size_t tbl_offset(int nt, int m, int kc_n)
+{
+    return xh_offset(nt) + 64 + (size_t)m * kc_n * XQ4G_KCHUNK * 2;
+}
 __host__ __device__ inline size_t ring_offset(int nt, bool xh, int m, int kc_n)
 {
     size_t o = xh_offset(nt);
-    if (xh) o += 64 + (size_t)m * kc_n * XQ4G_KCHUNK * 2;  // 8 token exponents (+pad), fp16 x
+    if (xh) o = tbl_offset(nt, m, kc_n) + (size_t)kc_n * 64;  // + one float4 per (chunk, lane quad)
     return (o + 127) & ~(size_t)127;
 }
 __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
@@ -106,9 +119,10 @@ __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
 // per-chunk tests.  On the fp16 path xr points at the token's fp16 row in
 // shared memory (zero padded to whole chunks).
 template <int NT, bool SAFE, bool XH>
-__device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *full, uint32_t phase, int kc0,
-                                              int kc_n, int k, const uint16_t *const (&xr)[NT], int warp,
-                                              int lane, float (&acc)[NT][4])
+__device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, uint32_t phase, int kc0,
+                                              int kc_n, int k, const uint16_t *const (&xr)[NT],
+                                              const uint32_t (&xs)[NT], uint32_t tbl, int warp, int lane,
+                                              float (&acc)[NT][4])
 {
     // chunks whose activation runs are held in registers at once (bounds
     // the register file for 16-token tiles)
@@ -126,7 +140,7 @@ __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *fu
                 for (int G2 = 0; G2 < 2; G2++) {
                     const int kb = kc * XQ4G_KCHUNK + 32 * G2 + 8 * t;
                     if (XH) {
-                        xf[c][nt][G2] = (!SAFE || kc < kc_n) ? *reinterpret_cast<const uint4 *>(xr[nt] + kb)
+                        xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::lds_v4(xs[nt] + 2 * kb)
                                                              : make_uint4(0, 0, 0, 0);
                     } else if (!SAFE || (kc < kc_n && kb < k)) {
                         xf[c][nt][G2] = xq4d::ldg_v4(xr[nt] + kb);
@@ -136,15 +150,24 @@ __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *fu
                 }
         }
         if (c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
+        float4 zc[R];  // fp16 path: zero-point corrections of the chunk's two groups
+        if (XH) {
+#pragma unroll
+            for (int c = 0; c < R; c++) {
+                const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
+                zc[c] = (!SAFE || kc < kc_n) ? xq4d::lds_f4(tbl + 16 * (kc * 4 + t))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
         uint4 cw[R];
         uint2 sw[R];
 #pragma unroll
         for (int c = 0; c < R; c++) {
             const int cl = warp + (c0 + c) * kConsumerWarps;  // chunk within the stage
-            const uint8_t *up = stage + cl * XQ4G_UNIT_BYTES;
+            const uint32_t up = stage + cl * XQ4G_UNIT_BYTES;
             if (!SAFE || kc0 + cl < kc_n) {
-                cw[c] = *reinterpret_cast<const uint4 *>(up + lane * 16);
-                sw[c] = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+                cw[c] = xq4d::lds_v4(up + lane * 16);
+                sw[c] = xq4d::lds_v2(up + XQ4G_CODE_BYTES + g * 8);
             } else {
                 cw[c] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
                 sw[c] = make_uint2(0, 0);
@@ -160,9 +183,9 @@ __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *fu
                 float s_hi = __uint_as_float(sg & 0xFFFF0000u);  // row g+8
                 uint32_t a0[4], a1[4];
                 if (XH) {
-                    s_hi *= 0.0625f;  // rows g+8 carry 16*q (unpack_word_h16)
-                    xq4d::unpack_word_h16(words[2 * G2], a0);
-                    xq4d::unpack_word_h16(words[2 * G2 + 1], a1);
+                    s_hi *= 0.0625f;  // rows g+8 carry 16*c (unpack_word_c16)
+                    xq4d::unpack_word_c16(words[2 * G2], a0);
+                    xq4d::unpack_word_c16(words[2 * G2 + 1], a1);
                 } else {
                     xq4d::unpack_word_q(words[2 * G2], a0);
                     xq4d::unpack_word_q(words[2 * G2 + 1], a1);
@@ -171,7 +194,12 @@ __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *fu
                 for (int nt = 0; nt < NT; nt++) {
                     float tacc[4];
                     if (XH) {
-                        xq4d::mma_f16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
+                        // accumulator starts at -8 * sum(x) of the group
+                        // (x 2^-24; x 16 for rows g+8): the MMA then yields
+                        // 2^-24 * sum((c - 8) * x) = 2^-24 * sum(q * x)
+                        const float z0 = G2 ? zc[c].z : zc[c].x, z1 = G2 ? zc[c].w : zc[c].y;
+                        const float cin[4] = {z0, z1, 16.f * z0, 16.f * z1};
+                        xq4d::mma_f16_16816_c(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y, cin);
                         xq4d::mma_f16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
                     } else {
                         xq4d::mma_bf16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
@@ -184,6 +212,14 @@ __device__ __forceinline__ bool consume_stage(const uint8_t *stage, uint64_t *fu
         }
     }
     return true;
+}
+
+// Power-of-two exponent that brings a token's max |x| (bf16 magnitude bits)
+// into [2^14, 2^15); 0 for an all-zero token.
+__device__ __forceinline__ int tok_exponent(unsigned mx)
+{
+    const int ex = (int)(mx >> 7) - 127;  // exponent of the max
+    return mx == 0 ? 0 : min(max(14 - ex, -252), 254);
 }
 
 // 2^e as a product of two normal floats (e in [-252, 254]).
@@ -205,8 +241,9 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     uint64_t *red_full = empty + kStages;     // [kRedBufs]: all 16 partials written
     uint64_t *red_free = red_full + kRedBufs;  // [kRedBufs]: reduction done, buffer reusable
     float *red = reinterpret_cast<float *>(smem + kBarBytes);
-    int *tok_exp = reinterpret_cast<int *>(smem + xh_offset(NT));            // fp16 path: [8]
+    unsigned *tok_max = reinterpret_cast<unsigned *>(smem + xh_offset(NT));  // fp16 path: [8] max |x| bits
     uint16_t *xh = reinterpret_cast<uint16_t *>(smem + xh_offset(NT) + 64);  // fp16 path: [m][kp]
+    float4 *tbl = reinterpret_cast<float4 *>(smem + tbl_offset(NT, m, kc_n));  // fp16 path: [kc][4]
     uint8_t *ring = smem + ring_offset(NT, XH, m, kc_n);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -225,12 +262,14 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             xq4d::mbar_init(&red_full[b], kConsumerWarps);
             xq4d::mbar_init(&red_free[b], 1);
         }
+        if (XH)
+            for (int i = 0; i < 8; i++) tok_max[i] = 0;
         xq4d::fence_barrier_init();
     }
     __syncthreads();
     xq4d::grid_dep_launch();
 
-    if (warp == kConsumerWarps) {  // ------------------------------ producer
+    if (warp == kProducerWarp) {  // ------------------------------ producer
         if (lane == 0) {
             int slot = 0, rb = rb0, kc0 = 0;
             uint32_t phase = 0;
@@ -258,57 +297,125 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
         return;
     }
 
+    if (warp == kReducerWarp) {  // ------------------------------ reducer
+        // Row block rbl's 8 partials arrive in buffer rbl % kRedBufs; sum
+        // them in warp order (deterministic), write the 16 rows, free the
+        // buffer.  The consumers never wait for this unless all buffers are
+        // still being reduced.
+        xq4d::grid_dep_wait();
+        const float *red_c = red;
+        for (int rbl = 0; rbl < rb1 - rb0; rbl++) {
+            const int buf = rbl % kRedBufs;
+            const uint32_t use = (uint32_t)(rbl / kRedBufs);
+            if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
+                atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                return;
+            }
+            const float *rd = red_c + (size_t)buf * kConsumerWarps * NT * 128;  // [warp][tok][row]
+            const int rb = rb0 + rbl;
+            for (int o = lane; o < m * 16; o += 32) {  // o = tok * 16 + row
+                const int tok = o >> 4, r = o & 15;
+                float sum = 0.f;
+#pragma unroll
+                for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * NT * 128 + o];
+                const int row = rb * XQ4G_ROWS + r;
+                if (row < n) {
+                    if (XH) {  // undo 2^-24 and the token's power of two (exact)
+                        float f1, f2;
+                        pow2_split(24 - tok_exponent(tok_max[tok]), f1, f2);
+                        sum = sum * f1 * f2;
+                    }
+                    if (out_f32)
+                        reinterpret_cast<float *>(y)[(size_t)tok * n + row] = sum;
+                    else
+                        reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + row] = __float2bfloat16_rn(sum);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
+        }
+        return;
+    }
+
     // ------------------------------------------------------------ consumers
     xq4d::grid_dep_wait();  // x is written, y may be read, by the neighbouring kernels
 
     if (XH) {
         // Stage x as fp16 with a per-token power of two: max|x| * 2^e lies in
-        // [2^14, 2^15).  Every consumer thread takes 8-element runs (16 bytes);
-        // k is a multiple of 32, so runs never straddle a token.
-        const int runs = k / 8, kp_runs = kp / 8;
-        unsigned *tok_max = reinterpret_cast<unsigned *>(tok_exp);
-        if (threadIdx.x < 8) tok_max[threadIdx.x] = 0;
-        xq4d::named_bar_sync(1, kConsumerThreads);
-        for (int tok = 0; tok < m; tok++) {
+        // [2^14, 2^15).  One pass: every consumer thread loads its 16-byte
+        // runs of the flat [m][k] activation into registers (all loads in
+        // flight together), the per-token maxima meet in shared memory, and
+        // the same registers are scaled, converted and stored.  k is a
+        // multiple of 32, so a run never straddles a token.
+        constexpr int kRuns = (kXhMaxElems / 8 + kConsumerThreads - 1) / kConsumerThreads;
+        const int runs = k / 8, total_runs = m * runs;
+        uint4 v[kRuns];
+#pragma unroll
+        for (int j = 0; j < kRuns; j++) {
+            const int r = threadIdx.x + j * kConsumerThreads;
+            v[j] = r < total_runs ? xq4d::ldg_v4(x + 8 * (size_t)r) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < kRuns; j++) {
+            if (j * kConsumerThreads >= total_runs) break;  // uniform across the block
+            const int r = min(threadIdx.x + j * kConsumerThreads, total_runs - 1);
+            const int tok = r / runs;
+            const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
             unsigned mx = 0;  // max |x| as bf16 magnitude bits (ordered like the values)
-            for (int r = threadIdx.x; r < runs; r += kConsumerThreads) {
-                const uint4 v = xq4d::ldg_v4(x + (size_t)tok * k + 8 * r);
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int h = 0; h < 4; h++) mx = max(mx, max(w[h] & 0x7FFFu, (w[h] >> 16) & 0x7FFFu));
+            for (int h = 0; h < 4; h++) mx = max(mx, max(w[h] & 0x7FFFu, (w[h] >> 16) & 0x7FFFu));
+            const int tok0 = __shfl_sync(0xffffffffu, tok, 0);
+            if (__all_sync(0xffffffffu, tok == tok0)) {  // the warp's runs are one token's
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (lane == 0 && mx) atomicMax(&tok_max[tok0], mx);
+            } else if (mx) {
+                atomicMax(&tok_max[tok], mx);
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane == 0) atomicMax(&tok_max[tok], mx);
         }
+        float *tblf = reinterpret_cast<float *>(tbl);
+        for (int i = threadIdx.x; i < kc_n * 16; i += kConsumerThreads) tblf[i] = 0.f;
         xq4d::named_bar_sync(1, kConsumerThreads);
-        if (threadIdx.x < m) {
-            const unsigned mx = tok_max[threadIdx.x];
-            const int ex = (int)(mx >> 7) - 127;  // exponent of the max (bf16 bits)
-            tok_exp[threadIdx.x] = mx == 0 ? 0 : min(max(14 - ex, -252), 254);
-        }
-        xq4d::named_bar_sync(1, kConsumerThreads);
-        for (int tok = 0; tok < m; tok++) {
-            float f1, f2;
-            pow2_split(tok_exp[tok], f1, f2);
-            for (int r = threadIdx.x; r < kp_runs; r += kConsumerThreads) {
-                uint4 o = make_uint4(0, 0, 0, 0);
-                if (r < runs) {
-                    const uint4 v = xq4d::ldg_v4(x + (size_t)tok * k + 8 * r);
-                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-                    uint32_t h2[4];
+        // Convert, store, and sum each 32-K group of the staged values (the
+        // four runs of a group sit in four consecutive lanes): the zero-point
+        // correction table entry (chunk, lane quad t) holds -8 * 2^-24 *
+        // {X(G0, 2t), X(G0, 2t+1), X(G1, 2t), X(G1, 2t+1)}, X = group sum.
 #pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        const float lo = __uint_as_float(w[h] << 16) * f1 * f2;
-                        const float hi = __uint_as_float(w[h] & 0xFFFF0000u) * f1 * f2;
-                        const __half2 p = __floats2half2_rn(lo, hi);
-                        h2[h] = *reinterpret_cast<const uint32_t *>(&p);
-                    }
-                    o = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+        for (int j = 0; j < kRuns; j++) {
+            if (j * kConsumerThreads >= total_runs) break;  // uniform across the block
+            const int r = threadIdx.x + j * kConsumerThreads;
+            float part = 0.f;
+            int tok = 0, kk = 0;
+            if (r < total_runs) {
+                tok = r / runs;
+                kk = 8 * (r - tok * runs);
+                float f1, f2;
+                pow2_split(tok_exponent(tok_max[tok]), f1, f2);
+                const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+                uint32_t h2[4];
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const float lo = __uint_as_float(w[h] << 16) * f1 * f2;
+                    const float hi = __uint_as_float(w[h] & 0xFFFF0000u) * f1 * f2;
+                    const __half2 p = __floats2half2_rn(lo, hi);
+                    h2[h] = *reinterpret_cast<const uint32_t *>(&p);
+                    const float2 pf = __half22float2(p);
+                    part += pf.x + pf.y;
                 }
-                *reinterpret_cast<uint4 *>(xh + (size_t)tok * kp + 8 * r) = o;
+                *reinterpret_cast<uint4 *>(xh + (size_t)tok * kp + kk) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            if (r < total_runs && (r & 3) == 0) {
+                const int grp = kk >> 5;  // group index along K
+                tblf[((grp >> 1) * 4 + (tok >> 1)) * 4 + (grp & 1) * 2 + (tok & 1)] = -8.f * 0x1p-24f * part;
             }
         }
+        // zero the K padding of every token (k % 64 == 32: one half chunk)
+        const int pad_runs = (kp - k) / 8;
+        for (int i = threadIdx.x; i < m * pad_runs; i += kConsumerThreads)
+            *reinterpret_cast<uint4 *>(xh + (size_t)(i / pad_runs) * kp + k + 8 * (i % pad_runs)) =
+                make_uint4(0, 0, 0, 0);
         xq4d::named_bar_sync(1, kConsumerThreads);
     }
 
@@ -317,11 +424,14 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     // output columns that are never written, so those lanes read token 0's
     // row instead of being predicated off.
     const uint16_t *xr[NT];
+    uint32_t xs[NT];  // fp16 path: shared addresses of the token rows
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
         const int tok = g + 8 * nt;
         xr[nt] = XH ? xh + (size_t)(tok < m ? tok : 0) * kp : x + (size_t)(tok < m ? tok : 0) * k;
+        xs[nt] = XH ? xq4d::smem_u32(xr[nt]) : 0u;
     }
+    const uint32_t tbl_s = xq4d::smem_u32(tbl), ring_s = xq4d::smem_u32(ring);
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
@@ -332,10 +442,10 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     uint32_t phase = 0;
     const bool k_whole = (k % XQ4G_KCHUNK) == 0;
     for (int i = 0; i < total; i++) {
-        const uint8_t *stage = ring + (size_t)slot * kStageBytes;
+        const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
         const bool fast = (XH || k_whole) && kc0 + kStageChunks <= kc_n;
-        const bool ok = fast ? consume_stage<NT, false, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc)
-                             : consume_stage<NT, true, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, warp, lane, acc);
+        const bool ok = fast ? consume_stage<NT, false, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc)
+                             : consume_stage<NT, true, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc);
         if (!ok) {
             atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
             return;
@@ -350,9 +460,8 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 
         if (kc0 >= kc_n) {  // ------------------------------ row block complete
             // Every warp leaves its partial in buffer rbl % kRedBufs and moves
-            // on; warp rbl % 16 waits for all 16 partials, sums them in warp
-            // order (deterministic) and writes the row block.  A warp waits
-            // only before reusing a buffer whose reduction is still running.
+            // on; the reducer warp sums them.  A warp waits only before
+            // reusing a buffer whose reduction is still running.
             kc0 = 0;
             const int buf = rbl % kRedBufs;
             const uint32_t use = (uint32_t)(rbl / kRedBufs);
@@ -372,33 +481,6 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             }
             __syncwarp();
             if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);
-            if (warp == rbl % kConsumerWarps) {  // this row block's reducer
-                if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
-                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
-                    return;
-                }
-                const int rb = rb0 + rbl;
-                for (int o = lane; o < m * 16; o += 32) {  // o = tok * 16 + row
-                    const int tok = o >> 4, r = o & 15;
-                    float s = 0.f;
-#pragma unroll
-                    for (int w = 0; w < kConsumerWarps; w++) s += rd[(size_t)w * NT * 128 + o];
-                    const int row = rb * XQ4G_ROWS + r;
-                    if (row < n) {
-                        if (XH) {  // undo the token's power of two (exact)
-                            float f1, f2;
-                            pow2_split(-tok_exp[tok], f1, f2);
-                            s = s * f1 * f2;
-                        }
-                        if (out_f32)
-                            reinterpret_cast<float *>(y)[(size_t)tok * n + row] = s;
-                        else
-                            reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + row] = __float2bfloat16_rn(s);
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
-            }
             rbl++;
         }
     }
@@ -455,12 +537,13 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
 }  // namespace
 
 // m in 1..16 per launch; larger m is split into 16-token slices.
-cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
-                            int out_f32, cudaStream_t st)
+cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y, int out_f32,
+                            const xq4_gemv_ws &ws, cudaStream_t st)
 {
+    (void)ws;
     static_assert(xh_offset(2) + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem, "bf16 plan too large");
-    static_assert(xh_offset(1) + 64 + 2 * (size_t)kXhMaxElems + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem,
-                  "fp16 plan too large");
+    static_assert(xh_offset(1) + 64 + (size_t)kXhMaxBytes + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem / 2 - 1024,
+                  "fp16 plan too large for two CTAs per SM");
     const size_t ysz = out_f32 ? 4 : 2;
     const int kp = xq4g_kc(k) * XQ4G_KCHUNK;
     const uint8_t *p = reinterpret_cast<const uint8_t *>(pack);
@@ -469,7 +552,7 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
         const uint16_t *xs = reinterpret_cast<const uint16_t *>(x) + (size_t)t0 * k;
         void *ys = reinterpret_cast<char *>(y) + (size_t)t0 * n * ysz;
         cudaError_t e;
-        if (mt <= 8 && (size_t)mt * kp <= (size_t)kXhMaxElems)
+        if (xh_fits(mt, kp))
             e = launch_one<1, true>(p, n, k, xs, mt, ys, out_f32, st);
         else if (mt <= 8)
             e = launch_one<1, false>(p, n, k, xs, mt, ys, out_f32, st);
@@ -479,6 +562,13 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
     }
     return cudaSuccess;
 }
+
+size_t xq4_gemv_ws_bytes(int n, int ctas)
+{
+    return (size_t)ctas * 2 * 2 * 128 * sizeof(float) + (size_t)xq4g_nb(n) * sizeof(unsigned);
+}
+
+int xq4_gemv_ws_ctas() { return sm_count_of_current_device() * kCtasPerSm; }
 
 // Read and clear this unit's fault word on the current device.
 unsigned int xq4_take_fault_gemv()

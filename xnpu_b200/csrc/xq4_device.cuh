@@ -135,6 +135,35 @@ __device__ __forceinline__ void unpack_word_h16(uint32_t w, uint32_t (&a)[4])
     a[3] = fma_f16x2(lop3_and_or(w8, 0x00F000F0u, kMagic), kOne, kNeg1152);
 }
 
+// Unpack one XQ4G code word into the four f16x2 mma A-fragment registers as
+// fp16 subnormals: a half whose bits are a nibble value v (exponent field 0)
+// is exactly v * 2^-24, so masking alone yields
+//   w & 0x000F000F -> c * 2^-24          (rows g)
+//   w & 0x00F000F0 -> 16 c * 2^-24       (rows g+8)
+// and the same on w >> 8 for nibbles 2/3: one shift and four ANDs per word.
+// The codes are c = q + 8; the caller removes the 8 * sum(x) this adds
+// through the MMA's accumulator input.
+__device__ __forceinline__ void unpack_word_c16(uint32_t w, uint32_t (&a)[4])
+{
+    const uint32_t w8 = w >> 8;
+    a[0] = w & 0x000F000Fu;
+    a[1] = w & 0x00F000F0u;
+    a[2] = w8 & 0x000F000Fu;
+    a[3] = w8 & 0x00F000F0u;
+}
+
+// D = A(16x16, row) * B(16x8, col) + C, f16 in, f32 accumulate.
+__device__ __forceinline__ void mma_f16_16816_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                                const float (&c)[4])
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %12, %13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
 // D = A(16x16, row) * B(16x8, col), f16 in, f32 out (zero accumulator).
 __device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
@@ -241,6 +270,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     for (uint32_t i = 0; i < limit; i++)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
+}
+
+// Shared-memory loads by 32-bit shared address (explicit ld.shared: the
+// short-latency path, whatever the compiler can infer about a pointer).
+__device__ __forceinline__ uint4 lds_v4(uint32_t a)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a)
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t a)
+{
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 lds_f4(uint32_t a)
+{
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a)
+                 : "memory");
+    return v;
 }
 
 // Bulk global -> shared copy (no multicast), completion counted on `bar`.

@@ -21,6 +21,14 @@ int xq4_repack_rows(const void *src, size_t src_len, const xq4_layout_desc *desc
 #include <cuda_runtime.h>
 
 // A weight resident in HBM, in XQ4G layout.
+// Decode-GEMV workspace of one weight: split-row-block partials and one
+// arrival counter per row block (zero between launches).
+struct xq4_gemv_ws {
+    float *part;
+    unsigned *cnt;
+    int ctas;          // largest grid the partial area holds
+};
+
 struct xq4_weight {
     struct xq4_device *dev;
     int ordinal;       // device ordinal (destroy does not touch `dev`)
@@ -28,12 +36,18 @@ struct xq4_weight {
     int nb, kc;        // row blocks, 64-K chunks
     uint8_t *d_pack;   // xq4g_bytes(n, k) bytes
     size_t bytes;
+    void *d_ws;        // GEMV workspace allocation (xq4_gemv_ws_bytes)
+    struct xq4_gemv_ws ws;
 };
 
 // Kernel launchers (gemv.cu, gemm_tc.cu, dequant.cu).  All return cudaError_t
 // of the launch; arguments are validated by the callers in api.cu.
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
-                            int out_f32, cudaStream_t st);
+                            int out_f32, const struct xq4_gemv_ws &ws, cudaStream_t st);
+// Workspace bytes for an n-row weight and a grid of `ctas` (partials first,
+// then nb counters), and the grid the current device runs the GEMV with.
+size_t xq4_gemv_ws_bytes(int n, int ctas);
+int xq4_gemv_ws_ctas();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
 cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);
