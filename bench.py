@@ -1,15 +1,18 @@
 """Benchmark of the B200 int4 (Q4NX / w4) decode path.
 
 Workload (one step = one token): the Llama-3-8B-shaped decode linear set at
-batch 1 -- 32 layers x {QKV 4096->6144, O 4096->4096, gate 4096->14336,
-up 4096->14336, down 14336->4096} -- with independent seeded random int4
-weights per layer (group 32, bf16 scales |N(0,0.02)|/7.5, zero point 8) and
+batch 1 -- 32 layers x {QKV 4096->6144, O 4096->4096, gate+up 4096->2x14336,
+down 14336->4096} -- with independent seeded random int4 weights per layer (group 32, bf16 scales |N(0,0.02)|/7.5, zero point 8) and
 bf16 N(0,1) activations; each projection reads a fixed activation, as the
 reference's projection-stream benchmark does (crates/xnpu-cli/src/main.rs:
 2487-2499, :3288).  3.93 GB of weights per step, far above the 126 MB L2, so
 no flush is needed between steps.
 
-On N GPUs (torchrun, one process per GPU) the FFN gate/up projections are
+Gate and up are one fused "gateup" projection, as in the reference's own
+layer chain (crates/xnpu-cli/src/main.rs:2464, :2488: 4 GEMV shapes per
+layer, qkv / o / gateup / down); the weight bytes are those of the two.
+
+On N GPUs (torchrun, one process per GPU) the FFN gateup projection is
 column-sharded N ways and their outputs all-gathered over NCCL each layer;
 QKV, O and down are replicated.  The step is the same token, so scaling is
 "strong".  The line also reports the lm_head 4096->128256 (f32 logits)
@@ -35,8 +38,14 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 LAYERS = 32
-SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate", 14336, 4096), ("up", 14336, 4096),
-          ("down", 4096, 14336)]
+SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gateup", 28672, 4096), ("down", 4096, 14336)]
+SHARDED = ("gateup",)  # column-sharded over ranks; the rest are replicas
+# DRAM bytes (read + write) per launch of each projection at one GPU, from
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#       --clock-control none -k regex:gemv --csv python bench.py --layers 4 --steps 1
+#       --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
+# (every launch of the capture; the figures repeat to within 0.01 %).
+DRAM_PER_LAUNCH = {"qkv": 14231808, "o": 9512960, "gateup": 66216960, "down": 33126912}
 LMHEAD = (128256, 4096)
 
 
@@ -103,7 +112,7 @@ class ClockSampler:
 def cpu_baseline(steps=1, budget_s=12.0):
     """The reference's CPU path (oracle restatement of main.rs:2287-2296 over
     the L1 layout, rows split over all host threads) on a row sample of one
-    layer's five projections; scaled to tokens/s of the 32-layer set."""
+    layer's four projections; scaled to tokens/s of the 32-layer set."""
     from oracle import oracle as O
     from xnpu_b200 import synth
     threads = os.cpu_count() or 1
@@ -130,7 +139,7 @@ def cpu_baseline(steps=1, budget_s=12.0):
             break
     tok_s = 1.0 / (np.median(t_layer) * LAYERS)
     return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"1/16 of the rows of each of the 5 projections of one layer (L1 layout, sequential "
+            "sample": f"1/16 of the rows of each of the 4 projections of one layer (L1 layout, sequential "
                       f"f32 per row), {len(t_layer)} timed pass(es), scaled to 32 layers",
             "gbs": sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS * tok_s / 1e9}
 
@@ -151,7 +160,7 @@ def run_reference(args, rank, world):
             "dtype": "int4 weights, bf16 x, f32 accumulate", "data": "synthetic (seeded)",
             "impl": "reference",
             "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
-                                   "gate/up 4096x14336, down 14336x4096), M=1", "group": 32},
+                                   "gateup 4096x28672, down 14336x4096), M=1", "group": 32},
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
                              "sample": r["sample"]},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -160,7 +169,7 @@ def run_reference(args, rank, world):
 
 # ---------------------------------------------------------------- GPU arm
 def make_weights(dev, rank, world, seed_base=1):
-    """All 32 layers' weights; gate/up rows sharded over ranks."""
+    """All 32 layers' weights; gateup rows sharded over ranks."""
     from concurrent.futures import ThreadPoolExecutor
     from xnpu_b200 import hal, synth
 
@@ -171,7 +180,7 @@ def make_weights(dev, rank, world, seed_base=1):
         scales = synth.synth_scales(n, k, seed)
         src = synth.planes_bytes(codes, scales)
         r0, r1 = 0, 0
-        if world > 1 and name in ("gate", "up"):
+        if world > 1 and name in SHARDED:
             r0, r1 = rank * n // world, (rank + 1) * n // world
         return hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=r0, row_end=r1), src
 
@@ -256,7 +265,7 @@ def main():
         for layer in weights:
             for name, n, k in SHAPES:
                 w = layer[name]
-                if comm is not None and name in ("gate", "up"):
+                if comm is not None and name in SHARDED:
                     check(L.xq4_linear_sharded(comm, w.handle, xs[k].data_ptr(), ys[name].data_ptr(), None, 1, 0, st))
                 else:
                     check(L.xq4_linear_raw(w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
@@ -268,7 +277,7 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # warm-up (eager), then capture one step into a CUDA graph: 160 launches
+    # warm-up (eager), then capture one step into a CUDA graph: 128 launches
     # per token are too many to issue from the host at HBM speed
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -304,7 +313,7 @@ def main():
     # (per GPU) over the timed region's duration
     gpu_step_bytes = 0
     for name, n, k in SHAPES:
-        ns = n // world if (world > 1 and name in ("gate", "up")) else n
+        ns = n // world if (world > 1 and name in SHARDED) else n
         gpu_step_bytes += algo_bytes(ns, k) * LAYERS
     achieved = gpu_step_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
@@ -342,15 +351,18 @@ def main():
             "dtype": "int4 weights (u4 codes, bf16 scales), bf16 x, f32 accumulate",
             "data": "synthetic (seeded PCG64; random-init 8B-shaped weights)",
             "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
-                                   "gate/up 4096x14336, down 14336x4096), M=1",
+                                   "gateup 4096x28672, down 14336x4096), M=1",
                        "group": 32, "layers": LAYERS, "batch": 1,
-                       "parallelism": "single GPU" if world == 1 else f"gate/up column-sharded x{world} + NCCL all-gather; qkv/o/down replicated",
+                       "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world} + NCCL all-gather; qkv/o/down replicated",
                        "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
             "gbs": step_bytes * (1e3 / ms) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "kernel": "gemv_kernel<1> (decode GEMV, m=1)",
-                         "traffic": None,
+                         "traffic": (sum(DRAM_PER_LAUNCH[nm] for nm, _, _ in SHAPES) / len(SHAPES)
+                                     if world == 1 else None),
+                         "traffic_unit": "bytes per launch, mean over the step's projections (ncu)",
+                         "algorithmic_bytes_per_launch": gpu_step_bytes / LAYERS / len(SHAPES),
                          "region": "all GEMV launches of the timed steps (CUDA graph replays)",
                          "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()}},
             "e2e": e2e,
@@ -375,7 +387,7 @@ def main():
 
 def e2e_run(dev, weights, comm, world, args):
     """Same step through the public C ABI with host buffers: one pinned H2D of
-    the step's activations, 160 xq4_linear submits on the device queue, one
+    the step's activations, 128 xq4_linear submits on the device queue, one
     D2H of every output, xq4_wait -- timed on the host clock."""
     import ctypes
     import torch
@@ -403,7 +415,7 @@ def e2e_run(dev, weights, comm, world, args):
         check(L.xq4_buffer_upload(xb.handle, hx.data_ptr(), 0, x_bytes))
         for li, layer in enumerate(weights):
             for name, n, k in SHAPES:
-                if comm is not None and name in ("gate", "up"):
+                if comm is not None and name in SHARDED:
                     xp = xb.device_ptr() + k_off[k]
                     yp = yb.device_ptr() + y_off[(li, name)]
                     check(L.xq4_linear_sharded(comm, layer[name].handle, xp, yp, None, 1, 0,
@@ -430,7 +442,7 @@ def e2e_run(dev, weights, comm, world, args):
     xb.destroy()
     yb.destroy()
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
-            "ms_per_step": dt * 1e3, "path": "xq4_buffer_upload -> 160 x xq4_linear -> xq4_wait -> "
+            "ms_per_step": dt * 1e3, "path": "xq4_buffer_upload -> 128 x xq4_linear -> xq4_wait -> "
                                              "xq4_buffer_download (pinned host buffers)"}
 
 

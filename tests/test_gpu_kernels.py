@@ -209,12 +209,12 @@ def test_gemv_parity_ragged(dev, n, k, m):
     assert_parity(y, oracle_rows(q, s, x, np.arange(n)), f"{n}x{k} m={m}")
 
 
-@pytest.mark.parametrize("m,k", [(1, 4096), (3, 4096), (2, 8192), (8, 2048), (4, 14336)])
-def test_gemv_extreme_activation_magnitudes(dev, m, k):
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 512), (3, 4096, 512), (2, 8192, 512), (8, 2048, 512),
+                                   (4, 14336, 512), (1, 4096, 24576), (3, 4096, 24576), (2, 2048, 49152)])
+def test_gemv_extreme_activation_magnitudes(dev, m, k, n):
     """Tokens whose activations span huge, tiny and mixed magnitudes (the
-    fp16-staged decode path rescales each token by a power of two; the bf16
-    path takes x as is)."""
-    n = 512
+    fp16-staged decode path, taken for large matrices -- n >= 24576 here --
+    rescales each token by a power of two; the bf16 path takes x as is)."""
     q = synth.unpack_codes_signed(synth.synth_codes(n, k, 700 + m))
     s = synth.synth_scales(n, k, 700 + m)
     rng = np.random.default_rng(701 + m)
@@ -225,11 +225,40 @@ def test_gemv_extreme_activation_magnitudes(dev, m, k):
     xf[0, ::97] *= 1e-12  # tiny values mixed into the huge token
     x = synth.f32_to_bf16_bits(xf)
     w = import_planes(dev, q, s)
-    y = hal.linear(w, to_dev_u16(x), out_dtype=torch.float32).cpu().numpy()
-    ref = O.gemv_q(q, s, x)
+    rows = row_subset(n, limit=1024)
+    y = hal.linear(w, to_dev_u16(x), out_dtype=torch.float32).cpu().numpy()[:, rows]
+    ref = O.gemv_q(q[rows], s[rows], x)
     for t in range(m):  # per token: each has its own scale
         max_rel, mae, _ = rel_metrics(y[t], ref[t])
         assert max_rel <= 1e-3, (t, mags[t], max_rel)
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_gemv_fp16_path_kat_exact(dev, m):
+    """The fp16-staged path (large matrices) on the known-answer data: every
+    product and partial sum is exact, so the outputs equal the exact result
+    bit for bit (the oracle's sums are exact here too)."""
+    n, k = 24576, 4096
+    q, s, x = O.kat_fill(n, k)
+    w = import_planes(dev, q, s)
+    xs = np.repeat(x[None, :], m, axis=0)
+    y = from_dev_bf16(hal.linear(w, to_dev_u16(xs)))
+    rows = row_subset(n, limit=1024)
+    expect = O.round_bf16(O.gemv_q(q[rows], s[rows], xs))
+    assert np.array_equal(y[:, rows], expect)
+
+
+@pytest.mark.parametrize("m", [1, 2, 5])
+def test_gemv_fp16_path_parity_gateup(dev, m):
+    """Fused gate+up projection 4096 -> 28672, the fp16-staged path."""
+    n, k = 28672, 4096
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, 210))
+    s = synth.synth_scales(n, k, 210)
+    x = synth.synth_x(m, k, 211 + m)
+    w = import_planes(dev, q, s)
+    y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
+    rows = row_subset(n, limit=768)
+    assert_parity(y[:, rows], oracle_rows(q, s, x, rows), f"m={m}")
 
 
 def test_gemv_f32_output(dev):

@@ -1,0 +1,108 @@
+"""Column (N) sharded linear on two GPUs: xq4_linear_sharded over NCCL.
+
+Two processes (one per GPU) import their row shard of one matrix, run the
+shard's GEMV (m < 16) or GEMM (m >= 16), all-gather the slices with NCCL and
+must both hold the full output, within the parity bars of the single-GPU
+tests against the oracle over the full matrix.  Skipped with fewer than two
+GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _rank_main(rank, world, id_q, res_q):
+    import ctypes
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root))
+    sys.path.insert(0, str(root / "tests"))
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+    from oracle import oracle as O
+    from xnpu_b200 import hal, lib, synth
+    from xnpu_b200._lib import check
+    from test_gpu_kernels import rel_metrics
+
+    torch.cuda.set_device(rank)
+    L = lib()
+    dev = hal.Device.open(rank)
+    uid = (ctypes.c_char * 128)()
+    if rank == 0:
+        check(L.xq4_comm_unique_id(ctypes.addressof(uid)))
+        for _ in range(world - 1):
+            id_q.put(bytes(uid))
+    else:
+        uid = (ctypes.c_char * 128).from_buffer_copy(id_q.get(timeout=60))
+    comm = ctypes.c_void_p()
+    check(L.xq4_comm_init(dev.handle, rank, world, ctypes.addressof(uid), ctypes.byref(comm)))
+    out = {}
+    try:
+        n, k = 4096, 4096
+        q = synth.unpack_codes_signed(synth.synth_codes(n, k, 55))
+        s = synth.synth_scales(n, k, 55)
+        ns = n // world
+        src = synth.planes_bytes(synth.pack_codes_signed(q), s)
+        w = hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=rank * ns,
+                                                          row_end=(rank + 1) * ns))
+        rows = np.arange(0, n, 7)
+        for m, f32 in ((1, 0), (1, 1), (3, 0), (20, 0)):
+            x = synth.synth_x(m, k, 56 + m)
+            xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+            yd = torch.empty((m, n), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
+            ws = torch.empty((m, n), dtype=yd.dtype, device="cuda")
+            st = torch.cuda.current_stream().cuda_stream
+            check(L.xq4_linear_sharded(comm, w.handle, xd.data_ptr(), yd.data_ptr(), ws.data_ptr(), m, f32, st))
+            torch.cuda.synchronize()
+            got = yd.float().cpu().numpy()[:, rows]
+            if m < 16:
+                ref = O.gemv_q(q[rows], s[rows], x)
+            else:
+                ref = O.gemv_bf16(O.dequant_planes(q[rows], s[rows]), x)
+            if not f32:
+                ref = synth.bf16_bits_to_f32(O.round_bf16(ref))
+            max_rel, mae, _ = rel_metrics(got, ref)
+            out[(m, f32)] = (max_rel, mae)
+        w.destroy()
+        res_q.put((rank, "ok", out))
+    except Exception as e:
+        res_q.put((rank, "error", repr(e)))
+        raise
+    finally:
+        L.xq4_comm_destroy(comm)
+        dev.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_linear_sharded_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    id_q, res_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, id_q, res_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    results = [res_q.get(timeout=5) for _ in range(2)]
+    assert all(p.exitcode == 0 for p in procs), (results, [p.exitcode for p in procs])
+    for rank, status, out in results:
+        assert status == "ok", (rank, out)
+        for (m, f32), (max_rel, mae) in out.items():
+            assert max_rel <= 1e-2 and mae <= 1e-3, (rank, m, f32, max_rel, mae)

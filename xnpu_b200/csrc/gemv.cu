@@ -27,14 +27,17 @@
 //    dequant op's output, dequant.cu); only the f32 summation order differs.
 //  * Unpack, bf16 path: one lop3 per pair (p = 128 + code, bf16 magic) after a
 //    shift of the word by 0/4/8/12, then fma.rn.bf16x2 (q = p - 136, exact).
-//  * Unpack, fp16 path (m <= 8 and m*k <= 16384, i.e. batch-1/few-token
-//    decode): fp16's 10-bit mantissa holds the nibbles at bits 0-3 and 4-7 of
-//    each half under one magic, so a word needs one shift instead of three
-//    (the integer ALU pipe is this kernel's limit).  x is staged once per CTA
-//    in shared memory as fp16 scaled by a per-token power of two chosen from
-//    the token's max |x| (exact for every value within 2^30 of that max;
-//    below it the fp16 rounding error is under 2^-40 of the max), and the
-//    output is scaled back by the inverse power of two (exact).
+//  * Unpack, fp16 path (few-token decode on large matrices: m <= 8, the
+//    staged activations fit, at least 96K chunks): codes enter the MMA as
+//    fp16 subnormals (a half whose bits are the nibble value v is exactly
+//    v * 2^-24), so a code word needs one shift and four ANDs; the zero
+//    point (q = c - 8) is removed through the MMA's accumulator input, which
+//    starts each group at -8 * sum(x) (group sums computed once per CTA).  x
+//    is staged once per CTA in shared memory as fp16 scaled by a per-token
+//    power of two chosen from the token's max |x| (exact for every value
+//    within 2^30 of that max; below it the fp16 rounding error is under
+//    2^-40 of the max); the output is scaled back by 2^24 and the inverse
+//    power of two (exact).
 //  * At the end of a row block each warp leaves its partial sums in one of
 //    three shared-memory buffers and carries on; a dedicated reducer warp
 //    waits for the 8 partials, sums them in fixed warp order (deterministic)
@@ -89,6 +92,11 @@ constexpr int kMaxSmem = 227 * 1024;
 // x plus the correction table (k_padded * (2m + 1) bytes) small enough that
 // two CTAs still fit on an SM.
 constexpr int kXhMaxElems = 20480;
+// The fp16 path's activation staging is a block-wide prologue of 1.5-4 us
+// on the critical path; it pays for itself only on large matrices (measured
+// on B200 at m = 1: 28672 x 4096 and 128256 x 4096 are faster with it,
+// 14336 x 4096, 6144 x 4096, 4096 x 4096 and 4096 x 14336 without).
+constexpr long long kXhMinChunks = 98304;
 constexpr int kXhMaxBytes = 46080;
 __host__ __device__ constexpr bool xh_fits(int m, int kp)
 {
@@ -552,7 +560,7 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
         const uint16_t *xs = reinterpret_cast<const uint16_t *>(x) + (size_t)t0 * k;
         void *ys = reinterpret_cast<char *>(y) + (size_t)t0 * n * ysz;
         cudaError_t e;
-        if (xh_fits(mt, kp))
+        if (xh_fits(mt, kp) && (long long)xq4g_nb(n) * xq4g_kc(k) >= kXhMinChunks)
             e = launch_one<1, true>(p, n, k, xs, mt, ys, out_f32, st);
         else if (mt <= 8)
             e = launch_one<1, false>(p, n, k, xs, mt, ys, out_f32, st);
