@@ -208,6 +208,26 @@ int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w_shard,
                        const void *x_dev, void *y_full_dev, void *ws_dev,
                        int m, int out_dtype, void *stream);
 
+/* No counterpart in the reference.  xq4_linear_sharded without a workspace
+ * and without allocating anything, for callers that cannot allocate device
+ * memory when they run the op: a serving engine that reserved the GPU's
+ * memory up front and refuses later allocations, a decode loop that cannot
+ * afford cudaMalloc/cudaFree (cudaFree synchronises the device), or a
+ * foreign-language caller with no device allocator.  For m > 1 the gather
+ * stages through a fixed scratch array of XQ4_NOALLOC_SCRATCH_BYTES inside
+ * the library (held by every GPU that loads it until the process exits);
+ * m * n_total * element size beyond that is rejected with XQ4_EINVAL.  The
+ * first call on a device looks up the array's device address (set-up): make
+ * that first call before any stream capture.  All calls share the array, so
+ * calls that overlap on the GPU race on it.  NCCL sets up a communicator's
+ * connections, and allocates its own buffers, at the communicator's first
+ * collective: run one collective on it (for instance one xq4_linear_sharded
+ * call) before relying on this entry point to allocate nothing. */
+#define XQ4_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w_shard,
+                               const void *x_dev, void *y_full_dev,
+                               int m, int out_dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

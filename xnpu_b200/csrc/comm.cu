@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
+#include <mutex>
 #include <new>
 #include <string.h>
 
@@ -162,6 +163,95 @@ extern "C" int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w, const voi
                                                          comm->nranks, m, ns);
         else
             shard_permute<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)ws_dev, (uint16_t *)y_full_dev,
+                                                            comm->nranks, m, ns);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard permute: %s", cudaGetErrorString(e));
+    }
+    return XQ4_OK;
+}
+
+// ------------------------------------------------------------------ no allocation
+// xq4_linear_sharded_noalloc: the same sharded linear for callers that cannot
+// allocate device memory at the time of the call -- a serving engine that has
+// reserved the GPU's memory for weights and KV cache up front and refuses
+// later allocations, a decode loop that cannot afford cudaMalloc/cudaFree
+// (cudaFree synchronises the whole device), or a foreign-language caller of
+// this C ABI with no device allocator of its own.  Instead of the caller's
+// workspace, the m > 1 gather stages through the fixed array below (8 MiB,
+// which every GPU that loads this library holds until the process exits).
+// Nothing in it needs to start at zero: each call writes the whole gather
+// region (local slice, then the all-gather) before the permute reads it.
+// Every call shares the array, so calls that overlap on the GPU (other
+// streams, other threads) race on it.
+static __device__ __align__(256) unsigned char g_xq4_noalloc_scratch[XQ4_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the scratch array on device `ordinal` (current), looked
+// up once per device.
+static int noalloc_scratch(int ordinal, void **out)
+{
+    static void *addr[64];
+    static bool ready[64];
+    static std::mutex mu;
+    if (ordinal < 0 || ordinal >= 64) return xq4_fail(XQ4_EINVAL, "device ordinal %d out of range", ordinal);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ready[ordinal]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_xq4_noalloc_scratch);
+        if (e != cudaSuccess)
+            return xq4_fail(XQ4_ECUDA, "cudaGetSymbolAddress(no-allocation scratch): %s", cudaGetErrorString(e));
+        addr[ordinal] = p;
+        ready[ordinal] = true;
+    }
+    *out = addr[ordinal];
+    return XQ4_OK;
+}
+
+extern "C" int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w, const void *x_dev,
+                                          void *y_full_dev, int m, int out_dtype, void *stream)
+{
+    xq4_clear_error();
+    if (!comm || !w || !x_dev || !y_full_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (m <= 0) return xq4_fail(XQ4_EINVAL, "m must be >= 1 (got %d)", m);
+    if (out_dtype != XQ4_OUT_BF16 && out_dtype != XQ4_OUT_F32)
+        return xq4_fail(XQ4_EINVAL, "unknown out_dtype %d", out_dtype);
+    const size_t esz = out_dtype == XQ4_OUT_F32 ? 4 : 2;
+    const int ns = w->n;
+    if ((ns * esz) % 16)
+        return xq4_fail(XQ4_EINVAL, "shard rows (%d) x element size must be a multiple of 16 bytes", ns);
+    const size_t need = m > 1 ? (size_t)m * ns * comm->nranks * esz : 0;
+    if (need > XQ4_NOALLOC_SCRATCH_BYTES)
+        return xq4_fail(XQ4_EINVAL,
+                        "m x n_total x element size = %zu bytes exceeds the %u-byte scratch of the no-allocation "
+                        "entry point (use xq4_linear_sharded with a workspace)",
+                        need, (unsigned)XQ4_NOALLOC_SCRATCH_BYTES);
+    if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_full_dev & 15))
+        return xq4_fail(XQ4_EINVAL, "x and y must be 16-byte aligned");
+    NcclApi *a = nccl_api();
+    if (!a->ok) return xq4_fail(XQ4_ENCCL, "libnccl.so.2 could not be loaded");
+    const int ordinal = xq4_device_ordinal(comm->dev);
+    cudaError_t e = cudaSetDevice(ordinal);
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    void *ws = nullptr;
+    if (m > 1)
+        if (int rc = noalloc_scratch(ordinal, &ws)) return rc;
+    cudaStream_t st = (cudaStream_t)stream;  // NULL = CUDA's default stream
+    const int f32 = out_dtype == XQ4_OUT_F32;
+    const ncclDataType_t dt = f32 ? ncclFloat32 : ncclBfloat16;
+    const size_t slice = (size_t)m * ns;  // elements per rank
+    char *gather = (char *)(m == 1 ? y_full_dev : ws);
+    void *mine = gather + (size_t)comm->rank * slice * esz;
+    e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
+               : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
+    ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
+    if (m > 1) {
+        const size_t total = slice * comm->nranks;
+        const unsigned blocks = (unsigned)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+        if (f32)
+            shard_permute<float><<<blocks, 256, 0, st>>>((const float *)ws, (float *)y_full_dev, comm->nranks, m, ns);
+        else
+            shard_permute<uint16_t><<<blocks, 256, 0, st>>>((const uint16_t *)ws, (uint16_t *)y_full_dev,
                                                             comm->nranks, m, ns);
         e = cudaGetLastError();
         if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard permute: %s", cudaGetErrorString(e));
