@@ -8,23 +8,36 @@
 // weights.
 //
 // One CTA computes a 128-feature x BN-token output tile (BN = 256 for long
-// inputs, m rounded up to 16 otherwise), streaming K in 64-wide stages:
-//  * producer warp: per stage, 8 cp.async.bulk copies of the tile's packed
-//    XQ4G units (8 row blocks x one 64-K chunk, 4.6 KB) and one TMA tensor
-//    load of the x tile (BN x 64 bf16, 128-byte swizzle; no multicast), both
-//    counted on the stage's mbarrier;
-//  * 4 dequant warps: unpack + RNE_bf16(q * s) (fma.rn.bf16x2, exact as in the
-//    dequant op) straight into the A operand tile in the canonical K-major
-//    128-byte-swizzle layout (each lane owns whole 16-byte swizzle chunks),
-//    fence.proxy.async, arrive;
-//  * MMA warp: one elected thread issues 4 tcgen05.mma (M=128, N=BN, K=16)
-//    per stage, A = dequantized weights, B = x, D in tensor memory, and a
-//    tcgen05.commit that releases the stage;
-//  * epilogue (the 4 dequant warps, one per 32-lane TMEM quarter):
-//    tcgen05.ld the 128 x BN f32 accumulator, round, store y.
+// inputs, m rounded up to 16 otherwise) over a range of K, in 64-wide stages,
+// with three independent shared-memory rings:
+//  * packed weights: P stages of 4 consecutive K chunks of the tile's 8 row
+//    blocks (8 contiguous 2.3 KB runs, 18 KB), one 3-D TMA load each (no
+//    multicast), filled ahead of use by the packed producer warp -- the
+//    weights are the HBM stream (measured: TMA loads of single 576-byte
+//    units ran at ~6 GB/s per CTA);
+//  * x: X stages of the BN x 64 bf16 activation tile (TMA, 128-byte
+//    swizzle, out-of-range rows/K zero filled), from the x producer warp;
+//  * A: A stages of the dequantized 128 x 64 bf16 weight tile.
+// Eight dequant warps (warp w = row block w of the tile) turn each packed
+// stage into RNE_bf16(q * s) (fma.rn.bf16x2, exact as in the dequant op),
+// stored straight into the A tile in the canonical K-major 128-byte-swizzle
+// layout, each lane writing whole 16-byte swizzle chunks in an order that
+// keeps every 8-lane phase on 8 distinct bank groups; fence.proxy.async;
+// arrive.  One thread of the MMA warp issues 4 tcgen05.mma (M=128, N=BN,
+// K=16) per stage into tensor memory and tcgen05.commit releases the A and x
+// stages.  The epilogue (the dequant warps: 32 TMEM lanes x half the columns
+// each) reads the accumulator with tcgen05.ld.
+//
+// Split-K: when the output has fewer tiles than the GPU has CTA slots (small
+// m), S CTAs of one thread-block cluster take S slices of K for the same
+// tile.  Each leaves its f32 partial tile in its own shared memory; after a
+// cluster handshake on mbarriers (bounded waits), CTA z sums column slice z of
+// all S partials in rank order through distributed shared memory
+// (deterministic) and writes y.  No global workspace.
+//
 // Every mbarrier wait is bounded; a wait that runs out sets g_xq4_fault, the
-// CTA skips the rest of its work, waits for its own MMAs (bounded) and frees
-// its tensor memory before it returns.
+// thread skips the rest of its work (never a barrier), waits for its own
+// MMAs (bounded) and the CTA frees its tensor memory before it returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -37,22 +50,26 @@
 
 namespace {
 
-constexpr int kTileN = 128;     // features per CTA (MMA M)
-constexpr int kTileK = 64;      // K per stage (one XQ4G chunk)
-constexpr int kStages = 3;
-constexpr int kDequantWarps = 4;
-constexpr int kThreads = (kDequantWarps + 2) * 32;  // + producer warp + MMA warp
-constexpr int kProducerWarp = kDequantWarps;
-constexpr int kMmaWarp = kDequantWarps + 1;
-constexpr int kATileBytes = kTileN * kTileK * 2;    // 16 KB bf16
-constexpr int kPackedBytes = (kTileN / XQ4G_ROWS) * XQ4G_UNIT_BYTES;  // 4608
+constexpr int kTileN = 128;                      // features per CTA (MMA M)
+constexpr int kTileK = 64;                       // K per stage (one XQ4G chunk)
+constexpr int kRb = kTileN / XQ4G_ROWS;          // row blocks per tile (8)
+constexpr int kDqWarps = 8;                      // dequant + epilogue warps
+constexpr int kPackWarp = 8, kXWarp = 9, kMmaWarp = 10;
+constexpr int kThreads = 11 * 32;
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kATileBytes = kTileN * kTileK * 2;  // 16 KB bf16
+constexpr int kPkChunks = 4;                     // K chunks per packed-weight stage
+constexpr int kPackedBytes = kRb * kPkChunks * XQ4G_UNIT_BYTES;  // 18 KB: 8 runs of 2.3 KB
+constexpr int kMaxSplit = 8;
+constexpr int kMaxSmem = 227 * 1024;
 
 __host__ __device__ constexpr int x_tile_bytes(int bn) { return bn * kTileK * 2; }
-// [x tiles | A tiles | packed | barriers | tmem address], x and A 1024-aligned
-__host__ __device__ constexpr size_t smem_bytes(int bn)
+__host__ __device__ constexpr int n_bars(int P, int X, int A) { return 2 * P + 2 * X + 2 * A + 3; }
+// [A tiles | x tiles | packed | mbarriers | tmem address], all from a 1024-aligned base
+__host__ __device__ constexpr size_t smem_bytes(int bn, int P, int X, int A)
 {
-    return 1024 /* alignment slack */ + (size_t)kStages * (x_tile_bytes(bn) + kATileBytes + kPackedBytes) +
-           (3 * kStages + 1) * 8 + 16;
+    return 1024 + (size_t)A * kATileBytes + (size_t)X * x_tile_bytes(bn) + (size_t)P * kPackedBytes +
+           (size_t)n_bars(P, X, A) * 8 + 16;
 }
 
 // ------------------------------------------------------------ tcgen05 helpers
@@ -91,13 +108,11 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar)
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16])
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8])
 {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -111,41 +126,114 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, int c2,
+                                            uint64_t *bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(xq4d::smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(xq4d::smem_u32(bar))
+        : "memory");
+}
+
 // 16-byte chunk j (0..7) of row r of a K-major 128-byte-swizzle tile.
 __device__ __forceinline__ uint32_t sw128_offset(int r, int j)
 {
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
 }
 
+// ------------------------------------------------------------ cluster helpers
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_saddr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_saddr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_saddr) : "memory");
+}
+// Bounded wait with cluster-scope acquire (sees peers' shared-memory writes
+// released by their arrivals).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity)
+{
+    for (uint32_t i = 0; i < (1u << 24); i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(xq4d::smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t cluster_saddr)
+{
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_saddr) : "memory");
+    return v;
+}
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void store_out(void *y, int out_f32, size_t idx, float v)
+{
+    if (out_f32)
+        reinterpret_cast<float *>(y)[idx] = v;
+    else
+        reinterpret_cast<__nv_bfloat16 *>(y)[idx] = __float2bfloat16_rn(v);
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ pack, int n, int k, int nb,
-            int kc_n, int m, int bn, void *__restrict__ y, int out_f32)
+gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, int n, int nb,
+            int kc_n, int m, int bn, int P, int X, int A, int S, void *__restrict__ y, int out_f32)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *xt = smem;                                           // [stage][bn][64] bf16, swizzled
-    uint8_t *at = xt + (size_t)kStages * x_tile_bytes(bn);        // [stage][128][64] bf16, swizzled
-    uint8_t *pk = at + (size_t)kStages * kATileBytes;             // [stage][8 units]
-    uint64_t *full = reinterpret_cast<uint64_t *>(pk + (size_t)kStages * kPackedBytes);
-    uint64_t *a_full = full + kStages;
-    uint64_t *empty = a_full + kStages;
-    uint64_t *acc_full = empty + kStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    uint8_t *at = smem;                                     // [A][128][64] bf16, swizzled
+    uint8_t *xt = at + (size_t)A * kATileBytes;             // [X][bn][64] bf16, swizzled
+    uint8_t *pk = xt + (size_t)X * x_tile_bytes(bn);        // [P][8 units]
+    uint64_t *pfull = reinterpret_cast<uint64_t *>(pk + (size_t)P * kPackedBytes);
+    uint64_t *pempty = pfull + P;
+    uint64_t *xfull = pempty + P;
+    uint64_t *xempty = xfull + X;
+    uint64_t *afull = xempty + X;
+    uint64_t *aempty = afull + A;
+    uint64_t *accf = aempty + A;
+    uint64_t *part_ready = accf + 1;  // split-K: arrivals of the S CTAs' partials
+    uint64_t *part_done = part_ready + 1;  // split-K: the S CTAs finished reading
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(part_done + 1);
+    float *part = reinterpret_cast<float *>(smem);  // split-K partial [bn][128] over the A/x rings
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_n = blockIdx.x, tile_m = blockIdx.y;
-    const int rb0 = tile_n * (kTileN / XQ4G_ROWS);
-    const int nrb = min(kTileN / XQ4G_ROWS, nb - rb0);  // row blocks in this tile
+    const int tile_n = blockIdx.x, tile_m = blockIdx.y, z = blockIdx.z;
+    const int rb0 = tile_n * kRb;
     const int m0 = tile_m * bn;
+    const int kc_beg = (int)((long long)z * kc_n / S), kc_end = (int)((long long)(z + 1) * kc_n / S);
+    const int nk = kc_end - kc_beg;
     const uint32_t tmem_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
-            xq4d::mbar_init(&full[s], 1);
-            xq4d::mbar_init(&a_full[s], kDequantWarps * 32);
-            xq4d::mbar_init(&empty[s], 1);
+        for (int s = 0; s < P; s++) {
+            xq4d::mbar_init(&pfull[s], 1);
+            xq4d::mbar_init(&pempty[s], kDqWarps);
         }
-        xq4d::mbar_init(acc_full, 1);
+        for (int s = 0; s < X; s++) {
+            xq4d::mbar_init(&xfull[s], 1);
+            xq4d::mbar_init(&xempty[s], 1);
+        }
+        for (int s = 0; s < A; s++) {
+            xq4d::mbar_init(&afull[s], kDqWarps);
+            xq4d::mbar_init(&aempty[s], 1);
+        }
+        xq4d::mbar_init(accf, 1);
+        xq4d::mbar_init(part_ready, S);
+        xq4d::mbar_init(part_done, S);
         xq4d::fence_barrier_init();
     }
     if (warp == kMmaWarp) {  // allocate the accumulator columns
@@ -156,117 +244,208 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict_
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    if (S > 1)
+        cluster_sync_all();  // every CTA of the cluster has initialised its barriers
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool failed = false;
 
-    if (warp == kProducerWarp) {  // ------------------------------ producer
+    // Ring positions advance incrementally (slot, phase parity): no integer
+    // division by the runtime ring depths in the loops.
+    if (warp == kPackWarp) {  // ------------------------------ packed-weight producer
         if (lane == 0) {
-            const uint32_t bytes = (uint32_t)nrb * XQ4G_UNIT_BYTES + (uint32_t)x_tile_bytes(bn);
-            int issued = 0;
-            for (int kc = 0; kc < kc_n && !failed; kc++) {
-                const int s = kc % kStages;
-                const uint32_t fill = (uint32_t)(kc / kStages);
-                if (fill > 0 && !xq4d::mbar_wait(&empty[s], (fill - 1) & 1)) {
+            const int npk = (nk + kPkChunks - 1) / kPkChunks;
+            int s = 0, issued = 0;
+            uint32_t ph = 0;
+            for (int i = 0; i < npk; i++) {
+                if (i >= P && !xq4d::mbar_wait(&pempty[s], ph ^ 1)) {
                     failed = true;
                     break;
                 }
-                xq4d::mbar_arrive_expect_tx(&full[s], bytes);
-                for (int u = 0; u < nrb; u++)
-                    xq4d::bulk_g2s(pk + (size_t)s * kPackedBytes + u * XQ4G_UNIT_BYTES,
-                                   pack + ((size_t)(rb0 + u) * kc_n + kc) * XQ4G_UNIT_BYTES, XQ4G_UNIT_BYTES,
-                                   &full[s]);
-                tma_load_2d(xt + (size_t)s * x_tile_bytes(bn), &xmap, kc * kTileK, m0, &full[s]);
-                issued = kc + 1;
+                // chunks past this CTA's K range are loaded and ignored; past
+                // the matrix they read as zero
+                xq4d::mbar_arrive_expect_tx(&pfull[s], kPackedBytes);
+                tma_load_3d(pk + (size_t)s * kPackedBytes, &pmap, 0, kc_beg + i * kPkChunks, rb0, &pfull[s]);
+                issued = i + 1;
+                if (++s == P) {
+                    s = 0;
+                    ph ^= 1;
+                }
             }
             // no copy may still be landing in shared memory when the CTA exits
-            for (int kc = max(0, issued - kStages); kc < issued; kc++)
-                if (!xq4d::mbar_wait(&full[kc % kStages], (uint32_t)(kc / kStages) & 1)) failed = true;
+            for (int i = max(0, issued - P); i < issued; i++)
+                if (!xq4d::mbar_wait(&pfull[i % P], (uint32_t)(i / P) & 1)) failed = true;
+        }
+    } else if (warp == kXWarp) {  // ------------------------------ activation producer
+        if (lane == 0) {
+            const uint32_t bytes = (uint32_t)x_tile_bytes(bn);
+            int s = 0, issued = 0;
+            uint32_t ph = 0;
+            for (int i = 0; i < nk; i++) {
+                if (i >= X && !xq4d::mbar_wait(&xempty[s], ph ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                xq4d::mbar_arrive_expect_tx(&xfull[s], bytes);
+                tma_load_2d(xt + (size_t)s * x_tile_bytes(bn), &xmap, (kc_beg + i) * kTileK, m0, &xfull[s]);
+                issued = i + 1;
+                if (++s == X) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            for (int i = max(0, issued - X); i < issued; i++)
+                if (!xq4d::mbar_wait(&xfull[i % X], (uint32_t)(i / X) & 1)) failed = true;
         }
     } else if (warp == kMmaWarp) {  // ------------------------------ MMA issuer
         if (lane == 0) {
             const uint32_t idesc = idesc_bf16(kTileN, bn);
-            for (int kc = 0; kc < kc_n && !failed; kc++) {
-                const int s = kc % kStages;
-                const uint32_t par = (uint32_t)(kc / kStages) & 1;
-                if (!xq4d::mbar_wait(&full[s], par) || !xq4d::mbar_wait(&a_full[s], par)) {
+            const uint32_t a_base = xq4d::smem_u32(at), x_base = xq4d::smem_u32(xt);
+            int sx = 0, sa = 0;
+            uint32_t px = 0, pa = 0;
+            for (int i = 0; i < nk; i++) {
+                if (!xq4d::mbar_wait(&xfull[sx], px) || !xq4d::mbar_wait(&afull[sa], pa)) {
                     failed = true;
                     break;
                 }
                 tc_fence_after();
-                const uint64_t adesc = sw128_desc(xq4d::smem_u32(at + (size_t)s * kATileBytes));
-                const uint64_t bdesc = sw128_desc(xq4d::smem_u32(xt + (size_t)s * x_tile_bytes(bn)));
+                const uint64_t adesc = sw128_desc(a_base + (uint32_t)sa * kATileBytes);
+                const uint64_t bdesc = sw128_desc(x_base + (uint32_t)sx * (uint32_t)x_tile_bytes(bn));
 #pragma unroll
                 for (int kk = 0; kk < kTileK / 16; kk++)  // +32 bytes along K per step
-                    mma_bf16_ss(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kc | kk) != 0);
-                mma_commit(&empty[s]);  // stage free once these MMAs have read it
+                    mma_bf16_ss(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0);
+                mma_commit(&aempty[sa]);  // A stage free once these MMAs have read it
+                mma_commit(&xempty[sx]);  // x stage likewise
+                if (++sx == X) {
+                    sx = 0;
+                    px ^= 1;
+                }
+                if (++sa == A) {
+                    sa = 0;
+                    pa ^= 1;
+                }
             }
-            mma_commit(acc_full);  // accumulator complete (or whatever was issued)
+            mma_commit(accf);  // accumulator complete (or whatever was issued)
         }
-    } else {  // ------------------------------------------------ dequant + epilogue
+    } else {  // ------------------------------------------------ dequant (warp = row block)
         const int g = lane >> 2, t = lane & 3;
-        for (int kc = 0; kc < kc_n && !failed; kc++) {
-            const int s = kc % kStages;
-            if (!xq4d::mbar_wait(&full[s], (uint32_t)(kc / kStages) & 1)) {
+        const int gsel = g & 1;  // store order: keeps each 8-lane phase on 8 distinct chunk columns
+        int sp = 0, c = 0, sa = 0;  // packed stage slot, chunk within it, A slot
+        uint32_t pp = 0, pa = 0;
+        for (int i = 0; i < nk && !failed; i++) {
+            if (c == 0 && !xq4d::mbar_wait(&pfull[sp], pp)) {
                 failed = true;
                 break;
             }
-            uint8_t *a = at + (size_t)s * kATileBytes;
-#pragma unroll
-            for (int uu = 0; uu < 2; uu++) {  // this warp's two row blocks of the tile
-                const int u = warp * 2 + uu;
-                uint4 cw = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 0
-                uint2 sw = make_uint2(0, 0);
-                if (u < nrb) {
-                    const uint8_t *up = pk + (size_t)s * kPackedBytes + u * XQ4G_UNIT_BYTES;
-                    cw = *reinterpret_cast<const uint4 *>(up + lane * 16);
-                    sw = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
-                }
-                const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-                for (int G = 0; G < 2; G++) {
-                    const uint32_t sg = G ? sw.y : sw.x;
-                    const uint32_t s_lo = __byte_perm(sg, 0, 0x1010), s_hi = __byte_perm(sg, 0, 0x3232);
-                    uint32_t a0[4], a1[4];
-                    xq4d::dequant_word(words[2 * G], s_lo, s_hi, a0);
-                    xq4d::dequant_word(words[2 * G + 1], s_lo, s_hi, a1);
-                    // rows g / g+8 of row block u: K 32G+8t .. +8 = swizzle chunk 4G+t
-                    const int r0 = u * 16 + g, j = 4 * G + t;
-                    *reinterpret_cast<uint4 *>(a + sw128_offset(r0, j)) = make_uint4(a0[0], a0[2], a1[0], a1[2]);
-                    *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, j)) = make_uint4(a0[1], a0[3], a1[1], a1[3]);
+            // the box lands as [row block][chunk][576 B]
+            const uint8_t *up = pk + (size_t)sp * kPackedBytes + (warp * kPkChunks + c) * XQ4G_UNIT_BYTES;
+            const uint4 cw = *reinterpret_cast<const uint4 *>(up + lane * 16);
+            const uint2 sw = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+            __syncwarp();
+            const bool stage_done = c == kPkChunks - 1 || i == nk - 1;
+            if (lane == 0 && stage_done) xq4d::mbar_arrive(&pempty[sp]);  // packed stage read: refill it
+            if (++c == kPkChunks) {
+                c = 0;
+                if (++sp == P) {
+                    sp = 0;
+                    pp ^= 1;
                 }
             }
-            // each writer makes its stores visible to the tensor core, then arrives
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            xq4d::mbar_arrive(&a_full[s]);
-        }
-        // epilogue: TMEM lane = feature (32 per warp), column = token
-        if (!xq4d::mbar_wait(acc_full, 0)) failed = true;
-        if (!failed) {
-            tc_fence_after();
-            const int f = warp * 32 + lane;
-            const int feat = rb0 * XQ4G_ROWS + f;
-            for (int c0 = 0; c0 < bn; c0 += 16) {
-                uint32_t r[16];
-                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
+            if (i >= A && !xq4d::mbar_wait(&aempty[sa], pa ^ 1)) {
+                failed = true;
+                break;
+            }
+            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+            uint4 lo[2], hi[2];  // rows g / g+8, K 32G+8t .. +8 for group G
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
+            for (int G = 0; G < 2; G++) {
+                const uint32_t sg = G ? sw.y : sw.x;
+                const uint32_t s_lo = __byte_perm(sg, 0, 0x1010), s_hi = __byte_perm(sg, 0, 0x3232);
+                uint32_t a0[4], a1[4];
+                xq4d::dequant_word(words[2 * G], s_lo, s_hi, a0);
+                xq4d::dequant_word(words[2 * G + 1], s_lo, s_hi, a1);
+                lo[G] = make_uint4(a0[0], a0[2], a1[0], a1[2]);
+                hi[G] = make_uint4(a0[1], a0[3], a1[1], a1[3]);
+            }
+            uint8_t *a = at + (size_t)sa * kATileBytes;
+            const int r0 = warp * XQ4G_ROWS + g;  // swizzle chunk of (row, group G) = 4G + t
+            *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * gsel + t)) = gsel ? lo[1] : lo[0];
+            *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * (1 - gsel) + t)) = gsel ? lo[0] : lo[1];
+            *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * gsel + t)) = gsel ? hi[1] : hi[0];
+            *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * (1 - gsel) + t)) = gsel ? hi[0] : hi[1];
+            // each writer makes its stores visible to the tensor core; one
+            // arrival per warp (256 arrivals on one mbarrier serialise: they
+            // cost ~1 us per stage, measured)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(&afull[sa]);
+            if (++sa == A) {
+                sa = 0;
+                pa ^= 1;
+            }
+        }
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    // Dequant warp w reads TMEM lanes 32*(w%4).. (features) and columns
+    // [h*bn/2, (h+1)*bn/2) (tokens), h = w / 4.
+    const bool epi = warp < kDqWarps;
+    if (epi) {
+        if (!xq4d::mbar_wait(accf, 0)) failed = true;
+        tc_fence_after();
+        const int q4 = warp & 3, h = warp >> 2;
+        const int f = q4 * 32 + lane;  // feature within the tile = TMEM lane
+        const int feat = rb0 * XQ4G_ROWS + f;
+        const int c_half = bn / 2;
+        for (int c0 = h * c_half; c0 < (h + 1) * c_half; c0 += 8) {
+            uint32_t r[8];
+            tmem_ld8(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const float v = failed ? 0.f : __uint_as_float(r[c]);
+                if (S > 1) {
+                    part[(size_t)(c0 + c) * kTileN + f] = v;
+                } else {
                     const int tok = m0 + c0 + c;
-                    if (tok < m && feat < n && f < nrb * XQ4G_ROWS) {
-                        const float v = __uint_as_float(r[c]);
-                        if (out_f32)
-                            reinterpret_cast<float *>(y)[(size_t)tok * n + feat] = v;
-                        else
-                            reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + feat] = __float2bfloat16_rn(v);
-                    }
+                    if (!failed && tok < m && feat < n) store_out(y, out_f32, (size_t)tok * n + feat, v);
                 }
             }
         }
     }
+    if (S > 1) {
+        // Split-K: every CTA of the cluster signals that its partial is in
+        // place, then CTA z sums column slice z of the S partials in rank
+        // order and writes it; a CTA leaves only after every peer has
+        // finished reading its shared memory.
+        asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
+        if (threadIdx.x == 0) {
+            asm volatile("fence.acq_rel.cluster;" ::: "memory");
+            for (int r = 0; r < S; r++) remote_arrive(cluster_map(xq4d::smem_u32(part_ready), (uint32_t)r));
+        }
+        if (epi) {
+            if (!mbar_wait_cluster(part_ready, 0)) failed = true;
+            const int c_lo = (int)((long long)z * bn / S), c_hi = (int)((long long)(z + 1) * bn / S);
+            const int f = threadIdx.x & (kTileN - 1), feat = rb0 * XQ4G_ROWS + f;
+            const uint32_t part_s = xq4d::smem_u32(part);
+            for (int c = c_lo + (threadIdx.x >> 7); c < c_hi; c += kDqThreads / kTileN) {
+                const uint32_t off = (uint32_t)((c * kTileN + f) * 4);
+                float sum = 0.f;
+                for (int r = 0; r < S; r++) sum += ld_cluster_f32(cluster_map(part_s + off, (uint32_t)r));
+                const int tok = m0 + c;
+                if (!failed && tok < m && feat < n) store_out(y, out_f32, (size_t)tok * n + feat, sum);
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
+        if (threadIdx.x == 0) {
+            for (int r = 0; r < S; r++) remote_arrive(cluster_map(xq4d::smem_u32(part_done), (uint32_t)r));
+            if (!mbar_wait_cluster(part_done, 0)) failed = true;
+        }
+    }
     if (failed) atomicOr(&g_xq4_fault, XQ4_FAULT_GEMM_WAIT);
     // no MMA may still be writing the accumulator when it is freed
-    if (warp == kMmaWarp && lane == 0) xq4d::mbar_wait(acc_full, 0);
+    if (warp == kMmaWarp && lane == 0) xq4d::mbar_wait(accf, 0);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -289,6 +468,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
     return fn;
 }
 
+int sm_count()
+{
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = v > 0 ? v : 148;
+    }
+    return cache[dev];
+}
+
 }  // namespace
 
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y, int out_f32,
@@ -296,29 +489,89 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
 {
     auto encode = encode_fn();
     if (!encode) return cudaErrorNotSupported;
+    const int nb = xq4g_nb(n), kc = xq4g_kc(k);
     const int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
-    CUtensorMap map;
-    const cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
-    const cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kTileK, (cuuint32_t)bn};
-    const cuuint32_t estride[2] = {1, 1};
-    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), gdim, gstride, box,
-                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    // ring depths: deep weight prefetch, shallow x; two CTAs per SM up to bn = 64
+#ifndef XQ4_GEMM_ASLOTS
+#define XQ4_GEMM_ASLOTS 2
+#endif
+#ifndef XQ4_GEMM_XSMALL
+#define XQ4_GEMM_XSMALL 4
+#endif
+#ifndef XQ4_GEMM_PSMALL
+#define XQ4_GEMM_PSMALL 2
+#endif
+#ifndef XQ4_GEMM_XLARGE
+#define XQ4_GEMM_XLARGE 3
+#endif
+#ifndef XQ4_GEMM_PLARGE
+#define XQ4_GEMM_PLARGE 3
+#endif
+    const int A = XQ4_GEMM_ASLOTS;
+    const int P = bn <= 64 ? XQ4_GEMM_PSMALL : (bn <= 128 ? 4 : XQ4_GEMM_PLARGE);  // 18 KB packed stages
+    const int X = bn <= 64 ? XQ4_GEMM_XSMALL : XQ4_GEMM_XLARGE;
+    const size_t smem = smem_bytes(bn, P, X, A);
+    if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
+    const int per_sm = 2 * (smem + 1024) <= 228 * 1024 ? 2 : 1;
+
+    CUtensorMap xmap, pmap;
+    {
+        const cuuint64_t gdim[2] = {(cuuint64_t)k, (cuuint64_t)m};
+        const cuuint64_t gstride[1] = {(cuuint64_t)k * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)kTileK, (cuuint32_t)bn};
+        const cuuint32_t estride[2] = {1, 1};
+        if (encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(x), gdim, gstride, box, estride,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {
+        // XQ4G image as [row block][chunk][144 u32]: one box = 4 consecutive
+        // chunks of the 8 row blocks of a 128-feature tile (rows past nb and
+        // chunks past KC read as zero)
+        const cuuint64_t gdim[3] = {XQ4G_UNIT_BYTES / 4, (cuuint64_t)kc, (cuuint64_t)nb};
+        const cuuint64_t gstride[2] = {XQ4G_UNIT_BYTES, (cuuint64_t)kc * XQ4G_UNIT_BYTES};
+        const cuuint32_t box[3] = {XQ4G_UNIT_BYTES / 4, kPkChunks, kRb};
+        const cuuint32_t estride[3] = {1, 1, 1};
+        if (encode(&pmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t *>(pack), gdim, gstride, box,
+                   estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
-    const size_t smem = smem_bytes(256);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    const int nb = xq4g_nb(n), kc = xq4g_kc(k);
-    dim3 grid((nb + kTileN / XQ4G_ROWS - 1) / (kTileN / XQ4G_ROWS), (m + bn - 1) / bn);
-    gemm_kernel<<<grid, kThreads, smem_bytes(bn), st>>>(map, pack, n, k, nb, kc, m, bn, y, out_f32);
-    return cudaGetLastError();
+    const int tiles_n = (nb + kRb - 1) / kRb, tiles_m = (m + bn - 1) / bn;
+    const long long tiles = (long long)tiles_n * tiles_m;
+    // split K over a cluster when the tiles leave CTA slots idle; at least 4
+    // chunks per slice
+    int S = 1;
+    const long long slots = (long long)sm_count() * per_sm;
+    if (tiles < slots) {
+        S = (int)(slots / tiles);
+        if (S > kMaxSplit) S = kMaxSplit;
+        if (S > kc / 4) S = kc / 4;
+        if (S < 1) S = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles_n, tiles_m, S);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = S;
+    cfg.attrs = attr;
+    cfg.numAttrs = S > 1 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, X, A, S, y, out_f32);
 }
 
 unsigned int xq4_take_fault_gemm()

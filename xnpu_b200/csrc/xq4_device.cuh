@@ -263,13 +263,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity)
     return ok != 0;
 }
 
-// Bounded wait: false if the phase did not complete within `limit` polls
-// (each try_wait itself blocks for a hardware-defined interval).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: false if the phase did not complete within about 2 s.  A
+// waiting thread is suspended in the barrier (up to 20 us per try) instead of
+// spinning, so it leaves the issue slots to the warps doing the work.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 24))
 {
-    for (uint32_t i = 0; i < limit; i++)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+    (void)limit;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (global_ns() - t0 > 2000000000ull) return false;
+    }
 }
 
 // Shared-memory loads by 32-bit shared address (explicit ld.shared: the
