@@ -15,9 +15,12 @@
 //    multicast), filled ahead of use by the packed producer warp -- the
 //    weights are the HBM stream (measured: TMA loads of single 576-byte
 //    units ran at ~6 GB/s per CTA);
-//  * x: X stages of the BN x 64 bf16 activation tile (TMA, 128-byte
+//  * x: D stages of the BN x 64 bf16 activation tile (TMA, 128-byte
 //    swizzle, out-of-range rows/K zero filled), from the x producer warp;
-//  * A: A stages of the dequantized 128 x 64 bf16 weight tile.
+//  * A: D stages of the dequantized 128 x 64 bf16 weight tile.
+// The x and A rings advance together (depth D = 3), so one tcgen05.commit
+// per stage frees both (the MMA thread's issue rate bounds the loop: each
+// commit costs it ~125 ns, measured).
 // Eight dequant warps (warp w = row block w of the tile) turn each packed
 // stage into RNE_bf16(q * s) (fma.rn.bf16x2, exact as in the dequant op),
 // stored straight into the A tile in the canonical K-major 128-byte-swizzle
@@ -64,12 +67,12 @@ constexpr int kMaxSplit = 8;
 constexpr int kMaxSmem = 227 * 1024;
 
 __host__ __device__ constexpr int x_tile_bytes(int bn) { return bn * kTileK * 2; }
-__host__ __device__ constexpr int n_bars(int P, int X, int A) { return 2 * P + 2 * X + 2 * A + 3; }
+__host__ __device__ constexpr int n_bars(int P, int D) { return 2 * P + 3 * D + 3; }
 // [A tiles | x tiles | packed | mbarriers | tmem address], all from a 1024-aligned base
-__host__ __device__ constexpr size_t smem_bytes(int bn, int P, int X, int A)
+__host__ __device__ constexpr size_t smem_bytes(int bn, int P, int D)
 {
-    return 1024 + (size_t)A * kATileBytes + (size_t)X * x_tile_bytes(bn) + (size_t)P * kPackedBytes +
-           (size_t)n_bars(P, X, A) * 8 + 16;
+    return 1024 + (size_t)D * kATileBytes + (size_t)D * x_tile_bytes(bn) + (size_t)P * kPackedBytes +
+           (size_t)n_bars(P, D) * 8 + 16;
 }
 
 // ------------------------------------------------------------ tcgen05 helpers
@@ -191,20 +194,20 @@ __device__ __forceinline__ void store_out(void *y, int out_f32, size_t idx, floa
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, int n, int nb,
-            int kc_n, int m, int bn, int P, int X, int A, int S, void *__restrict__ y, int out_f32)
+            int kc_n, int m, int bn, int P, int D, int S, void *__restrict__ y, int out_f32)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *at = smem;                                     // [A][128][64] bf16, swizzled
-    uint8_t *xt = at + (size_t)A * kATileBytes;             // [X][bn][64] bf16, swizzled
-    uint8_t *pk = xt + (size_t)X * x_tile_bytes(bn);        // [P][8 units]
+    const int X = D, A = D;                                 // x and A stages advance together
+    uint8_t *at = smem;                                     // [D][128][64] bf16, swizzled
+    uint8_t *xt = at + (size_t)A * kATileBytes;             // [D][bn][64] bf16, swizzled
+    uint8_t *pk = xt + (size_t)X * x_tile_bytes(bn);        // [P][8 row blocks][4 chunks]
     uint64_t *pfull = reinterpret_cast<uint64_t *>(pk + (size_t)P * kPackedBytes);
     uint64_t *pempty = pfull + P;
     uint64_t *xfull = pempty + P;
-    uint64_t *xempty = xfull + X;
-    uint64_t *afull = xempty + X;
-    uint64_t *aempty = afull + A;
-    uint64_t *accf = aempty + A;
+    uint64_t *afull = xfull + X;
+    uint64_t *sfree = afull + A;  // stage d's x and A slots free again (one MMA commit)
+    uint64_t *accf = sfree + D;
     uint64_t *part_ready = accf + 1;  // split-K: arrivals of the S CTAs' partials
     uint64_t *part_done = part_ready + 1;  // split-K: the S CTAs finished reading
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(part_done + 1);
@@ -225,11 +228,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         }
         for (int s = 0; s < X; s++) {
             xq4d::mbar_init(&xfull[s], 1);
-            xq4d::mbar_init(&xempty[s], 1);
+            xq4d::mbar_init(&sfree[s], 1);
         }
         for (int s = 0; s < A; s++) {
             xq4d::mbar_init(&afull[s], kDqWarps);
-            xq4d::mbar_init(&aempty[s], 1);
         }
         xq4d::mbar_init(accf, 1);
         xq4d::mbar_init(part_ready, S);
@@ -284,7 +286,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             int s = 0, issued = 0;
             uint32_t ph = 0;
             for (int i = 0; i < nk; i++) {
-                if (i >= X && !xq4d::mbar_wait(&xempty[s], ph ^ 1)) {
+                if (i >= X && !xq4d::mbar_wait(&sfree[s], ph ^ 1)) {
                     failed = true;
                     break;
                 }
@@ -316,8 +318,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
 #pragma unroll
                 for (int kk = 0; kk < kTileK / 16; kk++)  // +32 bytes along K per step
                     mma_bf16_ss(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0);
-                mma_commit(&aempty[sa]);  // A stage free once these MMAs have read it
-                mma_commit(&xempty[sx]);  // x stage likewise
+                mma_commit(&sfree[sa]);  // x and A stage free once these MMAs have read it (sx == sa)
                 if (++sx == X) {
                     sx = 0;
                     px ^= 1;
@@ -353,7 +354,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                     pp ^= 1;
                 }
             }
-            if (i >= A && !xq4d::mbar_wait(&aempty[sa], pa ^ 1)) {
+            if (i >= A && !xq4d::mbar_wait(&sfree[sa], pa ^ 1)) {
                 failed = true;
                 break;
             }
@@ -492,25 +493,9 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
     const int nb = xq4g_nb(n), kc = xq4g_kc(k);
     const int bn = m >= 256 ? 256 : ((m + 15) / 16) * 16;
     // ring depths: deep weight prefetch, shallow x; two CTAs per SM up to bn = 64
-#ifndef XQ4_GEMM_ASLOTS
-#define XQ4_GEMM_ASLOTS 2
-#endif
-#ifndef XQ4_GEMM_XSMALL
-#define XQ4_GEMM_XSMALL 4
-#endif
-#ifndef XQ4_GEMM_PSMALL
-#define XQ4_GEMM_PSMALL 2
-#endif
-#ifndef XQ4_GEMM_XLARGE
-#define XQ4_GEMM_XLARGE 3
-#endif
-#ifndef XQ4_GEMM_PLARGE
-#define XQ4_GEMM_PLARGE 3
-#endif
-    const int A = XQ4_GEMM_ASLOTS;
-    const int P = bn <= 64 ? XQ4_GEMM_PSMALL : (bn <= 128 ? 4 : XQ4_GEMM_PLARGE);  // 18 KB packed stages
-    const int X = bn <= 64 ? XQ4_GEMM_XSMALL : XQ4_GEMM_XLARGE;
-    const size_t smem = smem_bytes(bn, P, X, A);
+    const int D = 3;                                   // x / A stages
+    const int P = bn <= 64 ? 2 : (bn <= 128 ? 4 : 3);  // 18 KB packed stages
+    const size_t smem = smem_bytes(bn, P, D);
     if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
     const int per_sm = 2 * (smem + 1024) <= 228 * 1024 ? 2 : 1;
 
@@ -571,7 +556,7 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
     attr[0].val.clusterDim.z = S;
     cfg.attrs = attr;
     cfg.numAttrs = S > 1 ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, X, A, S, y, out_f32);
+    return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, D, S, y, out_f32);
 }
 
 unsigned int xq4_take_fault_gemm()
