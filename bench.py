@@ -341,6 +341,9 @@ def main():
     # lm_head (sharded the same way), f32 logits
     lm = None if args.skip_lmhead else lmhead_run(dev, rank, world, comm, L, stream)
 
+    # W4A8 parity mode (the reference's NPU numerics) on the same step, 1 GPU
+    w4a8 = None if (args.skip_e2e or world > 1) else w4a8_run(weights, xs, stream, args)
+
     step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
     if rank == 0:
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
@@ -369,6 +372,7 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
             "lm_head": lm,
+            "w4a8": w4a8,
             "device": meta["name"],
         }
         if cpu is not None:
@@ -444,6 +448,52 @@ def e2e_run(dev, weights, comm, world, args):
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
             "ms_per_step": dt * 1e3, "path": "xq4_buffer_upload -> 128 x xq4_linear -> xq4_wait -> "
                                              "xq4_buffer_download (pinned host buffers)"}
+
+
+def w4a8_run(weights, xs, stream, args):
+    """The decode step in the W4A8 parity mode: per projection, quantize its
+    activation (xq4_quantize_x) and run the int8-activation GEMV
+    (xq4_linear_w4a8); CUDA-graph replays timed with events."""
+    import torch
+    from xnpu_b200 import lib
+    from xnpu_b200._lib import check
+    L = lib()
+    sp = stream.cuda_stream
+    qd = {k: (torch.empty((1, k), dtype=torch.int8, device="cuda"),
+              torch.empty((1, k // 32), dtype=torch.int16, device="cuda")) for k in xs}
+    ys = {name: torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for name, n, _ in SHAPES}
+
+    def step():
+        for layer in weights:
+            for name, n, k in SHAPES:
+                q, d = qd[k]
+                check(L.xq4_quantize_x(xs[k].data_ptr(), 1, k, q.data_ptr(), d.data_ptr(), 0, sp))
+                check(L.xq4_linear_w4a8(layer[name].handle, q.data_ptr(), d.data_ptr(), ys[name].data_ptr(), 1, 0,
+                                        sp))
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            g.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    del g
+    step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
+    return {"tok_s": 1e3 / ms, "ms_per_step": ms, "gbs": step_bytes / (ms * 1e-3) / 1e9,
+            "gpu_launches_per_step": 2 * len(SHAPES) * LAYERS,
+            "path": "per projection: xq4_quantize_x + xq4_linear_w4a8 (int8 activations, bf16 2048-K partials)"}
 
 
 def lmhead_run(dev, rank, world, comm, L, stream, reps=20):

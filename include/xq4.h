@@ -188,6 +188,23 @@ uint64_t xq4_last_seq(const xq4_device *dev);
  * (crates/xnpu-hal/src/ert.rs:147-165).  *bits = 0 means no fault. */
 int xq4_device_fault(xq4_device *dev, uint32_t *bits);
 
+/* ---------------------------------------------------------------- W4A8 parity mode */
+/* The reference's NPU numerics (its w4gemvu kernel takes int8 activations).
+ * Quantize bf16 x [m][k] (device) to int8 q [m][k] and bf16 group scales
+ * d [m][k/32]: per 32-K group d = RNE_bf16(max|x| / 127),
+ * q = clamp(round_half_even(x / d), -127, 127); an all-zero group gives q = 0,
+ * d = 0.  Bit-exact with w4u_quantize_x (crates/xnpu-cli/src/main.rs:
+ * 2955-2986).  Runs on CUDA device `device`, on `stream` (NULL = default). */
+int xq4_quantize_x(const void *x_dev, int m, int k, void *q_dev, void *d_dev, int device, void *stream);
+/* y[m][n] from the int8 activations of xq4_quantize_x: per 32-K group the
+ * exact int32 dot of q_x with the int4 weights, times f32(s_w) * f32(d_x),
+ * accumulated in f32 over each 2048-K chunk; each chunk partial is rounded
+ * to bf16 (the NPU writes its C tensor as bf16, main.rs:2912-2916) and the
+ * partials are summed in f32 in chunk order (w4u_read_c, main.rs:3066-3091),
+ * then rounded to out_dtype.  q must be 16-byte aligned. */
+int xq4_linear_w4a8(const xq4_weight *w, const void *q_dev, const void *d_dev, void *y_dev, int m,
+                    int out_dtype, void *stream);
+
 /* ---------------------------------------------------------------- shards */
 /* Column (N) sharding of large-N projections over P GPUs with an NCCL
  * all-gather of the outputs.  The reference is single-device; its nearest

@@ -42,6 +42,7 @@ _SIGS = {
     "q4o_kat_ref": (None, [_I, _I, _I, _u16p]),
     "q4o_quantize_x": (_I, [_u16p, _I, _i8p, _u16p]),
     "q4o_sum_chunk_partials": (None, [_u16p, _I, _I, _u16p]),
+    "q4o_gemv_w4a8": (_I, [_i8p, _u16p, _I, _I, _i8p, _u16p, _I, _f32p, _I]),
 }
 
 
@@ -232,3 +233,19 @@ def sum_chunk_partials(parts):
     out = np.empty(n, dtype=np.uint16)
     lib().q4o_sum_chunk_partials(_p(parts, _u16p), c, n, _p(out, _u16p))
     return out
+
+
+def gemv_w4a8(q, s, xq, dx, nthreads=8):
+    """f32 y[m][n] (before the final RNE) of the W4A8 parity-mode GEMV: int4
+    weights q [n][k] with bf16 scale bits s [n][k/32]; int8 activations xq
+    [m][k] with bf16 group scales dx [m][k/32] (from quantize_x)."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(s, dtype=np.uint16)
+    xq = np.ascontiguousarray(np.atleast_2d(xq), dtype=np.int8)
+    dx = np.ascontiguousarray(np.atleast_2d(dx), dtype=np.uint16)
+    n, k = q.shape
+    m = xq.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    _ok(lib().q4o_gemv_w4a8(_p(q, _i8p), _p(s, _u16p), n, k, _p(xq, _i8p), _p(dx, _u16p), m, _p(y, _f32p),
+                            nthreads), "gemv_w4a8")
+    return y

@@ -564,3 +564,68 @@ void q4o_sum_chunk_partials(const uint16_t *parts, int chunks, int n, uint16_t *
         out[i] = q4o_f32_to_bf16(acc);
     }
 }
+
+/* ------------------------------------------- W4A8 GEMV (parity mode)
+ * The reference's NPU arithmetic for the w4gemvu kernel (int8 activations
+ * from q4o_quantize_x, int4 weights; crates/xnpu-cli/src/main.rs:2912-2916:
+ * mmul<4,16,16,int8,int4>): per 32-K group an exact int32 dot
+ * T = sum q_w * q_x, scaled by the group's weight scale times the group's
+ * activation scale and accumulated in f32 over one 2048-K chunk,
+ * acc = fma(f32(s_w) * f32(d_x), f32(T), acc); each chunk's partial is
+ * rounded to bf16 (the C tensor holds bf16), and the partials are summed in
+ * f32 in chunk order (w4u_read_c, main.rs:3066-3091).  The order of the
+ * scale products inside the device kernel is not recorded in the reference
+ * (its IRON reference.py is not shipped); this restatement fixes it as above.
+ * y[m][n] is that f32 sum, before the final bf16 narrowing. */
+typedef struct {
+    const int8_t *qw; const uint16_t *sw; const int8_t *qx; const uint16_t *dx;
+    int n, k, m, r0, r1; float *y;
+} w4a8_job;
+
+static void *w4a8_rows(void *arg)
+{
+    const w4a8_job *j = (const w4a8_job *)arg;
+    const int ng = j->k / 32;
+    for (int t = 0; t < j->m; t++)
+        for (int i = j->r0; i < j->r1; i++) {
+            float total = 0.0f;
+            for (int c0 = 0; c0 < j->k; c0 += 2048) {
+                const int c1 = c0 + 2048 < j->k ? c0 + 2048 : j->k;
+                float acc = 0.0f;
+                for (int g = c0 / 32; g < c1 / 32; g++) {
+                    int32_t T = 0;
+                    for (int e = 0; e < 32; e++)
+                        T += (int32_t)j->qw[(size_t)i * j->k + g * 32 + e] *
+                             (int32_t)j->qx[(size_t)t * j->k + g * 32 + e];
+                    const float sd = q4o_bf16_to_f32(j->sw[(size_t)i * ng + g]) *
+                                     q4o_bf16_to_f32(j->dx[(size_t)t * ng + g]);
+                    acc = fmaf(sd, (float)T, acc);
+                }
+                const float part = q4o_bf16_to_f32(q4o_f32_to_bf16(acc));
+                total = c0 == 0 ? part : total + part;
+            }
+            j->y[(size_t)t * j->n + i] = total;
+        }
+    return NULL;
+}
+
+int q4o_gemv_w4a8(const int8_t *qw, const uint16_t *sw, int n, int k, const int8_t *qx,
+                  const uint16_t *dx, int m, float *y, int nthreads)
+{
+    if (m <= 0 || n <= 0 || k <= 0 || k % 32) return Q4O_EINVAL;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > 64) nthreads = 64;
+    if (nthreads > n) nthreads = n;
+    pthread_t th[64];
+    w4a8_job jobs[64];
+    const int per = (n + nthreads - 1) / nthreads;
+    int started = 0;
+    for (int t = 0; t < nthreads; t++) {
+        jobs[t] = (w4a8_job){qw, sw, qx, dx, n, k, m, t * per, (t + 1) * per < n ? (t + 1) * per : n, y};
+        if (jobs[t].r0 >= jobs[t].r1) break;
+        pthread_create(&th[t], NULL, w4a8_rows, &jobs[t]);
+        started++;
+    }
+    for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return Q4O_OK;
+}

@@ -99,6 +99,8 @@ SIGNATURES = {
     "xq4_comm_destroy": (_I, [_P]),
     "xq4_linear_sharded": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "xq4_linear_sharded_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "xq4_quantize_x": (_I, [_P, _I, _I, _P, _P, _I, _P]),
+    "xq4_linear_w4a8": (_I, [_P, _P, _P, _P, _I, _I, _P]),
 }
 
 _lib = None

@@ -307,6 +307,34 @@ extern "C" int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream)
     return XQ4_OK;
 }
 
+// ------------------------------------------------------------------ W4A8 parity mode
+extern "C" int xq4_quantize_x(const void *x_dev, int m, int k, void *q_dev, void *d_dev, int device, void *stream)
+{
+    xq4_clear_error();
+    if (!x_dev || !q_dev || !d_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (m <= 0 || k <= 0 || k % 32) return xq4_fail(XQ4_EINVAL, "m >= 1 and k a positive multiple of 32 (got m=%d k=%d)", m, k);
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    CK(xq4_launch_quantize_x(x_dev, m, k, q_dev, d_dev, (cudaStream_t)stream), "quantize launch");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_linear_w4a8(const xq4_weight *w, const void *q_dev, const void *d_dev, void *y_dev, int m,
+                               int out_dtype, void *stream)
+{
+    xq4_clear_error();
+    if (!w || !q_dev || !d_dev || !y_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (m <= 0) return xq4_fail(XQ4_EINVAL, "m must be >= 1 (got %d)", m);
+    if (out_dtype != XQ4_OUT_BF16 && out_dtype != XQ4_OUT_F32)
+        return xq4_fail(XQ4_EINVAL, "unknown out_dtype %d", out_dtype);
+    if (((uintptr_t)q_dev & 15) || (w->k % 16))
+        return xq4_fail(XQ4_EINVAL, "q must be 16-byte aligned");
+    CK(cudaSetDevice(w->ordinal), "cudaSetDevice");
+    cudaError_t e = xq4_launch_w4a8(w->d_pack, w->n, w->k, q_dev, d_dev, m, y_dev, out_dtype == XQ4_OUT_F32,
+                                    (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "w4a8 launch");
+    return XQ4_OK;
+}
+
 // ------------------------------------------------------------------ linear
 static int launch_linear(const xq4_weight *w, const void *x, void *y, int m, int out_dtype, cudaStream_t st)
 {
@@ -397,6 +425,6 @@ extern "C" int xq4_device_fault(xq4_device *dev, uint32_t *bits)
     if (!dev || !bits) return xq4_fail(XQ4_EINVAL, "NULL argument");
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     CK(cudaDeviceSynchronize(), "synchronize before reading the fault word");
-    *bits = xq4_take_fault_gemv() | xq4_take_fault_gemm();
+    *bits = xq4_take_fault_gemv() | xq4_take_fault_gemm() | xq4_take_fault_w4a8();
     return XQ4_OK;
 }

@@ -51,8 +51,12 @@ int xq4_gemv_ws_ctas();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
 cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);
+cudaError_t xq4_launch_quantize_x(const void *x, int m, int k, void *q, void *d, cudaStream_t st);
+cudaError_t xq4_launch_w4a8(const uint8_t *pack, int n, int k, const void *qx, const void *dx, int m, void *y,
+                            int out_f32, cudaStream_t st);
 unsigned int xq4_take_fault_gemv();
 unsigned int xq4_take_fault_gemm();
+unsigned int xq4_take_fault_w4a8();
 cudaStream_t xq4_device_cuda_stream(struct xq4_device *dev);
 int xq4_device_ordinal(const struct xq4_device *dev);
 #endif

@@ -251,6 +251,35 @@ def linear(weight, x, out_dtype=None, out=None, stream=None):
     return out
 
 
+def quantize_x(x, stream=None):
+    """W4A8 parity mode: int8 activations q [m, k] and bf16 group scales
+    d [m, k/32] (as int16 bits) of a CUDA bf16 tensor x [m, k]."""
+    import torch
+    if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] % 32:
+        raise ValueError("x must be a CUDA bf16 tensor [m, k] with k a multiple of 32")
+    x = x.contiguous()
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    d = torch.empty((m, k // 32), dtype=torch.int16, device=x.device)
+    check(lib().xq4_quantize_x(x.data_ptr(), m, k, q.data_ptr(), d.data_ptr(), x.device.index or 0,
+                               _torch_stream(stream)))
+    return q, d
+
+
+def linear_w4a8(weight, q, d, out_dtype=None, out=None, stream=None):
+    """W4A8 parity mode: y = the reference's int8-activation GEMV of (q, d)
+    from quantize_x against the weight."""
+    import torch
+    m = q.shape[0]
+    out_dtype = out_dtype or torch.bfloat16
+    code = XQ4_OUT_F32 if out_dtype == torch.float32 else XQ4_OUT_BF16
+    if out is None:
+        out = torch.empty((m, weight.n), dtype=out_dtype, device=q.device)
+    check(lib().xq4_linear_w4a8(weight.handle, q.contiguous().data_ptr(), d.contiguous().data_ptr(),
+                                out.data_ptr(), m, code, _torch_stream(stream)))
+    return out
+
+
 def dequant(weight, out=None, stream=None):
     """Dequantize the whole weight to a bf16 CUDA tensor [n, k]."""
     import torch
