@@ -208,9 +208,9 @@ def main():
                     help="layers of the weight set (32 = the benchmark; fewer only for profiler captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiler captures only")
     ap.add_argument("--skip-lmhead", action="store_true", help="profiler captures only")
-    ap.add_argument("--kernel-case", choices=["gemv", "gemm"],
+    ap.add_argument("--kernel-case", choices=["gemv", "gemm", "w4a8"],
                     help="profiler captures: one projection launched warmup+steps times on GPU 0 "
-                         "(gemv: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048)")
+                         "(gemv and w4a8: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048)")
     ap.add_argument("--case-m", type=int, default=None, help="token count of --kernel-case")
     args = ap.parse_args()
     if args.kernel_case:
@@ -553,7 +553,7 @@ def kernel_case(args):
     import torch
     from xnpu_b200 import hal, lib, synth
     from xnpu_b200._lib import check
-    n, k, m = (65536, 4096, 1) if args.kernel_case == "gemv" else (14336, 4096, 2048)
+    n, k, m = (14336, 4096, 2048) if args.kernel_case == "gemm" else (65536, 4096, 1)
     m = args.case_m or m
     dev = hal.Device.open(0)
     L = lib()
@@ -562,13 +562,22 @@ def kernel_case(args):
     x = torch.from_numpy(synth.synth_x(m, k, 32).view(np.int16)).cuda().view(torch.bfloat16)
     y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
     stream = torch.cuda.Stream()
+    q = torch.empty((m, k), dtype=torch.int8, device="cuda")
+    d = torch.empty((m, k // 32), dtype=torch.int16, device="cuda")
+
+    def one():
+        if args.kernel_case == "w4a8":
+            check(L.xq4_quantize_x(x.data_ptr(), m, k, q.data_ptr(), d.data_ptr(), 0, stream.cuda_stream))
+            check(L.xq4_linear_w4a8(w.handle, q.data_ptr(), d.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
+        else:
+            check(L.xq4_linear_raw(w.handle, x.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
     for _ in range(args.warmup):
-        check(L.xq4_linear_raw(w.handle, x.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
+        one()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     for _ in range(args.steps):
-        check(L.xq4_linear_raw(w.handle, x.data_ptr(), y.data_ptr(), m, 0, stream.cuda_stream))
+        one()
     b.record(stream)
     torch.cuda.synchronize()
     us = a.elapsed_time(b) * 1e3 / max(1, args.steps)
