@@ -13,8 +13,8 @@ layer chain (crates/xnpu-cli/src/main.rs:2464, :2488: 4 GEMV shapes per
 layer, qkv / o / gateup / down); the weight bytes are those of the two.
 
 On N GPUs (torchrun, one process per GPU) the FFN gateup projection is
-column-sharded N ways and their outputs all-gathered over NCCL each layer;
-QKV, O and down are replicated.  The step is the same token, so scaling is
+column-sharded N ways, with the all-gather inside the GEMV kernel over NVLink
+peer memory (xq4_linear_sharded_fused); QKV, O and down are replicated.  The step is the same token, so scaling is
 "strong".  The line also reports the lm_head 4096->128256 (f32 logits)
 sharded the same way.
 
@@ -266,7 +266,7 @@ def main():
             for name, n, k in SHAPES:
                 w = layer[name]
                 if comm is not None and name in SHARDED:
-                    check(L.xq4_linear_sharded(comm, w.handle, xs[k].data_ptr(), ys[name].data_ptr(), None, 1, 0, st))
+                    check(L.xq4_linear_sharded_fused(comm, w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
                 else:
                     check(L.xq4_linear_raw(w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
                 launches += 1
@@ -356,7 +356,7 @@ def main():
             "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
                                    "gateup 4096x28672, down 14336x4096), M=1",
                        "group": 32, "layers": LAYERS, "batch": 1,
-                       "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world} + NCCL all-gather; qkv/o/down replicated",
+                       "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world}, rows gathered by the GEMV over NVLink peer memory; qkv/o/down replicated",
                        "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
             "gbs": step_bytes * (1e3 / ms) / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -422,8 +422,8 @@ def e2e_run(dev, weights, comm, world, args):
                 if comm is not None and name in SHARDED:
                     xp = xb.device_ptr() + k_off[k]
                     yp = yb.device_ptr() + y_off[(li, name)]
-                    check(L.xq4_linear_sharded(comm, layer[name].handle, xp, yp, None, 1, 0,
-                                               dev.stream_handle()))
+                    check(L.xq4_linear_sharded_fused(comm, layer[name].handle, xp, yp, 1, 0,
+                                                     dev.stream_handle()))
                 else:
                     check(L.xq4_linear(dev.handle, layer[name].handle, xb.handle, k_off[k], yb.handle,
                                        y_off[(li, name)], 1, 0, ctypes.byref(seq)))
@@ -446,8 +446,9 @@ def e2e_run(dev, weights, comm, world, args):
     xb.destroy()
     yb.destroy()
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
-            "ms_per_step": dt * 1e3, "path": "xq4_buffer_upload -> 128 x xq4_linear -> xq4_wait -> "
-                                             "xq4_buffer_download (pinned host buffers)"}
+            "ms_per_step": dt * 1e3,
+            "path": "xq4_buffer_upload -> 128 x xq4_linear (gateup: xq4_linear_sharded_fused when N > 1) -> "
+                    "xq4_wait -> xq4_buffer_download (pinned host buffers)"}
 
 
 def w4a8_run(weights, xs, stream, args):
@@ -497,8 +498,9 @@ def w4a8_run(weights, xs, stream, args):
 
 
 def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
-    """lm_head 4096 -> 128256, f32 logits, rows sharded over ranks +
-    all-gather; 8 rotating weight copies (>2x L2 at every N)."""
+    """lm_head 4096 -> 128256, f32 logits, rows sharded over ranks and
+    gathered inside the GEMV over peer memory; 8 rotating weight copies
+    (>2x L2 at every N)."""
     import torch
     import torch.distributed as dist
     from xnpu_b200 import hal, synth
@@ -518,7 +520,7 @@ def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
 
     def go(i):
         if comm is not None:
-            check(L.xq4_linear_sharded(comm, ws[i % copies].handle, x.data_ptr(), y.data_ptr(), None, 1, 1, sp))
+            check(L.xq4_linear_sharded_fused(comm, ws[i % copies].handle, x.data_ptr(), y.data_ptr(), 1, 1, sp))
         else:
             check(L.xq4_linear_raw(ws[i % copies].handle, x.data_ptr(), y.data_ptr(), 1, 1, sp))
 
@@ -544,7 +546,7 @@ def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
         w.destroy()
     shard_bytes = algo_bytes(r1 - r0, k, out_bytes=4)
     return {"us": ms * 1e3, "shard_rows": r1 - r0, "gbs_per_gpu": shard_bytes / (ms * 1e-3) / 1e9,
-            "logits_allgather_bytes": n * 4 if world > 1 else 0}
+            "logits_gather_bytes_in": (n - (r1 - r0)) * 4}
 
 
 def kernel_case(args):

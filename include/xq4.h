@@ -225,6 +225,26 @@ int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w_shard,
                        const void *x_dev, void *y_full_dev, void *ws_dev,
                        int m, int out_dtype, void *stream);
 
+/* xq4_linear_sharded with the all-gather fused into the GEMV: each rank's
+ * kernel sends every output value it computes to every peer over NVLink, as
+ * one 64-bit word (value and call number) in the peer's inbox, and copies
+ * the peers' values for its own row range from its inbox into y_full, so
+ * when the call's work on a rank's stream completes, that rank's y_full
+ * (any device memory, m x n_total elements of out_dtype) holds every rank's
+ * rows.  m in 1..15 and m x n_total <= XQ4_FUSED_MAX_VALUES; every rank
+ * holds a shard of the same size and makes the same calls in the same
+ * order.  The first call on a communicator allocates and maps the inboxes
+ * (2 x XQ4_FUSED_MAX_VALUES x 8 bytes per rank, collective, device-wide
+ * synchronising): make it before any stream capture.  A peer value that
+ * does not arrive within 2 s sets fault bit 0x8 (xq4_device_fault).  Do not
+ * run the call beside other kernels that wait on peers: each CTA waits for
+ * the matching CTA of every peer.  Stands in for the column split with a host
+ * gather of the per-column C sections (w4u_read_c,
+ * crates/xnpu-cli/src/main.rs:3066-3091). */
+#define XQ4_FUSED_MAX_VALUES (4u * 1024u * 1024u)
+int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w_shard, const void *x_dev,
+                             void *y_full_dev, int m, int out_dtype, void *stream);
+
 /* No counterpart in the reference.  xq4_linear_sharded without a workspace
  * and without allocating anything, for callers that cannot allocate device
  * memory when they run the op: a serving engine that reserved the GPU's

@@ -1,10 +1,14 @@
-"""Column (N) sharded linear on two GPUs: xq4_linear_sharded over NCCL.
+"""Column (N) sharded linear on two GPUs.
 
 Two processes (one per GPU) import their row shard of one matrix, run the
-shard's GEMV (m < 16) or GEMM (m >= 16), all-gather the slices with NCCL and
-must both hold the full output, within the parity bars of the single-GPU
-tests against the oracle over the full matrix.  Skipped with fewer than two
-GPUs.
+shard's GEMV (m < 16) or GEMM (m >= 16), all-gather the slices with NCCL
+(xq4_linear_sharded) and must both hold the full output, within the parity
+bars of the single-GPU tests against the oracle over the full matrix.  For
+m < 16 the same call with the gather fused into the GEMV over peer memory
+(xq4_linear_sharded_fused) must give the identical bits on both ranks, twice
+in a row, with no fault bit raised; a fused call that only one rank makes
+must end after the kernel's bounded wait with fault bit 0x8, leaving the
+context usable.  Skipped with fewer than two GPUs.
 """
 import os
 import socket
@@ -77,6 +81,38 @@ def _rank_main(rank, world, id_q, res_q):
                 ref = synth.bf16_bits_to_f32(O.round_bf16(ref))
             max_rel, mae, _ = rel_metrics(got, ref)
             out[(m, f32)] = (max_rel, mae)
+            if m < 16:
+                # the same call with the gather fused into the GEMV over peer
+                # memory: identical bits on every rank, twice in a row (the
+                # two inbox halves)
+                for rep in range(2):
+                    yf = torch.full((m, n), float("nan"), dtype=yd.dtype, device="cuda")
+                    check(L.xq4_linear_sharded_fused(comm, w.handle, xd.data_ptr(), yf.data_ptr(), m, f32, st))
+                    torch.cuda.synchronize()
+                    iv = torch.int32 if f32 else torch.int16
+                    out[("fused", m, f32, rep)] = bool(torch.equal(yf.view(iv), yd.view(iv)))
+                bits = ctypes.c_uint32()
+                check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
+                out[("fault", m, f32)] = bits.value
+        # a peer that never makes the call: this rank's kernel gives up after
+        # its bounded wait (about 2 s), reports fault bit 0x8 and the context
+        # stays usable
+        if rank == 0:
+            x = synth.synth_x(1, k, 57)
+            xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+            yf = torch.empty((1, n), dtype=torch.bfloat16, device="cuda")
+            check(L.xq4_linear_sharded_fused(comm, w.handle, xd.data_ptr(), yf.data_ptr(), 1, 0, st))
+            torch.cuda.synchronize()
+            bits = ctypes.c_uint32()
+            check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
+            out[("lone_fault",)] = bits.value
+            yl = torch.empty((1, ns), dtype=torch.bfloat16, device="cuda")
+            check(L.xq4_linear_raw(w.handle, xd.data_ptr(), yl.data_ptr(), 1, 0, st))
+            torch.cuda.synchronize()
+            out[("lone_after",)] = bool(torch.equal(yl.view(torch.int16), yf[:, :ns].view(torch.int16)))
+            id_q.put("lone done")
+        else:
+            assert id_q.get(timeout=120) == "lone done"
         w.destroy()
         res_q.put((rank, "ok", out))
     except Exception as e:
@@ -104,5 +140,13 @@ def test_linear_sharded_two_gpus():
     assert all(p.exitcode == 0 for p in procs), (results, [p.exitcode for p in procs])
     for rank, status, out in results:
         assert status == "ok", (rank, out)
-        for (m, f32), (max_rel, mae) in out.items():
-            assert max_rel <= 1e-2 and mae <= 1e-3, (rank, m, f32, max_rel, mae)
+        for key, val in out.items():
+            if key[0] in ("fused", "lone_after"):
+                assert val, (rank, key, "fused gather differs from the NCCL path")
+            elif key[0] == "fault":
+                assert val == 0, (rank, key, val)
+            elif key[0] == "lone_fault":
+                assert val == 0x8, (rank, key, val)
+            else:
+                max_rel, mae = val
+                assert max_rel <= 1e-2 and mae <= 1e-3, (rank, key, max_rel, mae)

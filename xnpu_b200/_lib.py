@@ -31,6 +31,7 @@ XQ4_OUT_BF16 = 0
 XQ4_OUT_F32 = 1
 XQ4_UNIQUE_ID_BYTES = 128
 XQ4_NOALLOC_SCRATCH_BYTES = 8 * 1024 * 1024  # include/xq4.h
+XQ4_FUSED_MAX_VALUES = 4 * 1024 * 1024  # include/xq4.h
 
 _STATUS_NAMES = {
     XQ4_OK: "XQ4_OK", XQ4_EINVAL: "XQ4_EINVAL", XQ4_ENOMEM: "XQ4_ENOMEM", XQ4_ECUDA: "XQ4_ECUDA",
@@ -99,6 +100,7 @@ SIGNATURES = {
     "xq4_comm_destroy": (_I, [_P]),
     "xq4_linear_sharded": (_I, [_P, _P, _P, _P, _P, _I, _I, _P]),
     "xq4_linear_sharded_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "xq4_linear_sharded_fused": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "xq4_quantize_x": (_I, [_P, _I, _I, _P, _P, _I, _P]),
     "xq4_linear_w4a8": (_I, [_P, _P, _P, _P, _I, _I, _P]),
 }

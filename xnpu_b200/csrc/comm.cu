@@ -13,6 +13,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 #include <mutex>
+#include <vector>
 #include <new>
 #include <string.h>
 
@@ -68,11 +69,25 @@ __global__ void shard_permute(const T *__restrict__ ws, T *__restrict__ y, int n
 
 }  // namespace
 
+// A buffer every rank allocated together and mapped from every peer.
+struct shared_buf {
+    char *local;
+    size_t bytes;
+    char *peer[XQ4_MAX_RANKS];  // peer[rank] == local; others opened from IPC handles
+};
+
 struct xq4_comm {
     xq4_device *dev;
     ncclComm_t nccl;
     int rank, nranks;
+    // fused gather (created by the first xq4_linear_sharded_fused call): CTA
+    // count at 0, epoch at 4, the two inbox halves from kInboxHead
+    shared_buf inbox{};
+    void *xchg = nullptr;               // device scratch for exchanging IPC handles
 };
+
+static constexpr size_t kInboxHead = 256;
+static constexpr size_t kInboxHalfBytes = (size_t)XQ4_FUSED_MAX_VALUES * sizeof(unsigned long long);
 
 extern "C" int xq4_comm_unique_id(void *id_out)
 {
@@ -119,6 +134,21 @@ extern "C" int xq4_comm_destroy(xq4_comm *comm)
     if (!comm) return XQ4_OK;
     NcclApi *a = nccl_api();
     cudaSetDevice(xq4_device_ordinal(comm->dev));
+    if (comm->inbox.local) {
+        // every rank stops using its peers' memory before any rank frees its own
+        cudaDeviceSynchronize();
+        int one = 1;
+        int *d = (int *)comm->xchg;
+        cudaMemcpy(d, &one, sizeof one, cudaMemcpyHostToDevice);
+        a->AllGather(d, d + 16, 1, ncclInt32, comm->nccl, 0);
+        cudaDeviceSynchronize();
+        for (int r = 0; r < comm->nranks; r++)
+            if (r != comm->rank && comm->inbox.peer[r]) cudaIpcCloseMemHandle(comm->inbox.peer[r]);
+        a->AllGather(d, d + 16, 1, ncclInt32, comm->nccl, 0);
+        cudaDeviceSynchronize();
+        cudaFree(comm->inbox.local);
+    }
+    if (comm->xchg) cudaFree(comm->xchg);
     ncclResult_t r = a->CommDestroy(comm->nccl);
     delete comm;
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
@@ -256,5 +286,127 @@ extern "C" int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w, c
         e = cudaGetLastError();
         if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard permute: %s", cudaGetErrorString(e));
     }
+    return XQ4_OK;
+}
+
+// ------------------------------------------------------------------ peer-memory gather
+namespace {
+
+// Allocate `bytes` on every rank and map every peer's allocation (collective).
+int alloc_shared(xq4_comm *comm, size_t bytes, shared_buf *out)
+{
+    NcclApi *a = nccl_api();
+    shared_buf b{};
+    b.bytes = bytes;
+    cudaError_t e = cudaMalloc((void **)&b.local, bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for a shared buffer: %s", bytes, cudaGetErrorString(e));
+    }
+    cudaMemset(b.local, 0, bytes);
+    cudaIpcMemHandle_t mine, all[XQ4_MAX_RANKS];
+    e = cudaIpcGetMemHandle(&mine, b.local);
+    if (e != cudaSuccess) {
+        cudaFree(b.local);
+        return xq4_fail(XQ4_ECUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    }
+    char *x = (char *)comm->xchg;
+    cudaMemcpy(x, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    ncclResult_t r = a->AllGather(x, x + sizeof mine, sizeof mine, ncclUint8, comm->nccl, 0);
+    if (r != ncclSuccess) {
+        cudaFree(b.local);
+        return nccl_fail(r, "ncclAllGather(IPC handles)");
+    }
+    e = cudaMemcpy(all, x + sizeof mine, sizeof mine * comm->nranks, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        cudaFree(b.local);
+        return xq4_fail(XQ4_ECUDA, "IPC handle exchange: %s", cudaGetErrorString(e));
+    }
+    for (int q = 0; q < comm->nranks; q++) {
+        if (q == comm->rank) {
+            b.peer[q] = b.local;
+            continue;
+        }
+        void *p = nullptr;
+        e = cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int j = 0; j < q; j++)
+                if (j != comm->rank && b.peer[j]) cudaIpcCloseMemHandle(b.peer[j]);
+            cudaFree(b.local);
+            return xq4_fail(XQ4_ECUDA, "cudaIpcOpenMemHandle(rank %d): %s", q, cudaGetErrorString(e));
+        }
+        b.peer[q] = (char *)p;
+    }
+    *out = b;
+    return XQ4_OK;
+}
+
+}  // namespace
+
+namespace {
+
+// First fused call on a communicator: map every rank's inbox (collective).
+// The inbox is zeroed before its handle leaves this rank, so no peer writes
+// into it before that.
+int setup_inbox(xq4_comm *comm)
+{
+    cudaError_t e = cudaMalloc(&comm->xchg, 64 * 2 * (XQ4_MAX_RANKS + 1));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        comm->xchg = nullptr;
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc for the handle exchange: %s", cudaGetErrorString(e));
+    }
+    if (int rc = alloc_shared(comm, kInboxHead + 2 * kInboxHalfBytes, &comm->inbox)) {
+        cudaFree(comm->xchg);
+        comm->xchg = nullptr;
+        comm->inbox = shared_buf{};
+        return rc;
+    }
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "inbox set-up: %s", cudaGetErrorString(e));
+    return XQ4_OK;
+}
+
+}  // namespace
+
+extern "C" int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w, const void *x_dev, void *y_full_dev,
+                                        int m, int out_dtype, void *stream)
+{
+    xq4_clear_error();
+    if (!comm || !w || !x_dev || !y_full_dev) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (m <= 0 || m > 15) return xq4_fail(XQ4_EINVAL, "m must be in 1..15 (got %d)", m);
+    if (out_dtype != XQ4_OUT_BF16 && out_dtype != XQ4_OUT_F32)
+        return xq4_fail(XQ4_EINVAL, "unknown out_dtype %d", out_dtype);
+    if ((uintptr_t)x_dev & 15) return xq4_fail(XQ4_EINVAL, "x must be 16-byte aligned");
+    if (((uintptr_t)y_full_dev & 3) && out_dtype == XQ4_OUT_F32) return xq4_fail(XQ4_EINVAL, "y must be 4-byte aligned");
+    if ((uintptr_t)y_full_dev & 1) return xq4_fail(XQ4_EINVAL, "y must be 2-byte aligned");
+    if (comm->nranks > XQ4_MAX_RANKS) return xq4_fail(XQ4_ENOTSUP, "more than %d ranks", XQ4_MAX_RANKS);
+    const int ns = w->n;
+    const size_t values = (size_t)m * ns * comm->nranks;
+    if (values > XQ4_FUSED_MAX_VALUES)
+        return xq4_fail(XQ4_EINVAL, "m x n_total = %zu is above XQ4_FUSED_MAX_VALUES (%u)", values,
+                        (unsigned)XQ4_FUSED_MAX_VALUES);
+    cudaError_t e = cudaSetDevice(xq4_device_ordinal(comm->dev));
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    if (!comm->inbox.local && comm->nranks > 1)
+        if (int rc = setup_inbox(comm)) return rc;
+    xq4_p2p_out p{};
+    p.nranks = comm->nranks;
+    p.rank = comm->rank;
+    p.n_total = ns * comm->nranks;
+    p.row_off = ns * comm->rank;
+    if (comm->nranks > 1) {
+        for (int q = 0; q < comm->nranks; q++)
+            p.inbox[q] = (unsigned long long *)(comm->inbox.peer[q] + kInboxHead);
+        p.half_words = XQ4_FUSED_MAX_VALUES;
+        p.cnt = (unsigned *)comm->inbox.local;
+        p.epoch = (unsigned *)(comm->inbox.local + 4);
+        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32, w->ws,
+                            (cudaStream_t)stream, &p);
+    } else {  // one rank: the shard is the whole matrix
+        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32, w->ws,
+                            (cudaStream_t)stream);
+    }
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "fused sharded launch: %s", cudaGetErrorString(e));
     return XQ4_OK;
 }

@@ -238,10 +238,11 @@ __device__ __forceinline__ void pow2_split(int e, float &f1, float &f2)
     f2 = __int_as_float((e2 + 127) << 23);
 }
 
-template <int NT, bool XH>
+template <int NT, bool XH, bool P2P>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
-            const uint16_t *__restrict__ x, int m, void *__restrict__ y, int out_f32)
+            const uint16_t *__restrict__ x, int m, void *__restrict__ y, int out_f32,
+            const __grid_constant__ xq4_p2p_out p2p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -311,13 +312,19 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
         // buffer.  The consumers never wait for this unless all buffers are
         // still being reduced.
         xq4d::grid_dep_wait();
+        // P2P: this call's epoch (the previous fused launch on this rank
+        // completed before grid_dep_wait returned) and its inbox half
+        const unsigned e = P2P ? *reinterpret_cast<volatile const unsigned *>(p2p.epoch) + 1u : 0u;
+        const size_t half = P2P ? (size_t)(e & 1u) * p2p.half_words : 0;
         const float *red_c = red;
+        bool alive = true;
         for (int rbl = 0; rbl < rb1 - rb0; rbl++) {
             const int buf = rbl % kRedBufs;
             const uint32_t use = (uint32_t)(rbl / kRedBufs);
             if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
                 atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
-                return;
+                alive = false;  // P2P: still counted below, so the epoch advances
+                break;
             }
             const float *rd = red_c + (size_t)buf * kConsumerWarps * NT * 128;  // [warp][tok][row]
             const int rb = rb0 + rbl;
@@ -333,14 +340,70 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
                         pow2_split(24 - tok_exponent(tok_max[tok]), f1, f2);
                         sum = sum * f1 * f2;
                     }
-                    if (out_f32)
+                    if (P2P) {  // this rank's row: the local full output + one word per peer
+                        const size_t idx = (size_t)tok * p2p.n_total + p2p.row_off + row;
+                        uint32_t bits;
+                        if (out_f32) {
+                            reinterpret_cast<float *>(y)[idx] = sum;
+                            bits = __float_as_uint(sum);
+                        } else {
+                            const __nv_bfloat16 h = __float2bfloat16_rn(sum);
+                            reinterpret_cast<__nv_bfloat16 *>(y)[idx] = h;
+                            bits = __bfloat16_as_ushort(h);
+                        }
+                        const unsigned long long word = ((unsigned long long)e << 32) | bits;
+                        for (int q = 0; q < p2p.nranks; q++)
+                            if (q != p2p.rank) xq4d::st_sys_u64(p2p.inbox[q] + half + idx, word);
+                    } else if (out_f32) {
                         reinterpret_cast<float *>(y)[(size_t)tok * n + row] = sum;
-                    else
+                    } else {
                         reinterpret_cast<__nv_bfloat16 *>(y)[(size_t)tok * n + row] = __float2bfloat16_rn(sum);
+                    }
                 }
             }
             __syncwarp();
             if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
+        }
+        if (P2P) {
+            // The peers' rows of this CTA's row range (their CTA with the
+            // same index computes them: equal shards, equal grids), from the
+            // inbox into the full output.  Every CTA sends all its words
+            // before it waits, so no wait depends on a waiting CTA.
+            const int r0 = rb0 * XQ4G_ROWS, span = min(rb1 * XQ4G_ROWS, n) - r0;
+            const unsigned long long *in = p2p.inbox[p2p.rank] + half;
+            const int per_peer = m * span, total_w = (p2p.nranks - 1) * per_peer;
+            const uint64_t t0 = xq4d::global_ns();
+            bool ok = alive;
+            for (int i = lane; ok && i < total_w; i += 32) {
+                const int qi = i / per_peer, rem = i - qi * per_peer;
+                const int tok = rem / span, row = r0 + (rem - tok * span);
+                const int q = qi < p2p.rank ? qi : qi + 1;
+                const size_t idx = (size_t)tok * p2p.n_total + (size_t)q * n + row;
+                unsigned long long v = xq4d::ld_sys_u64(in + idx);
+                while ((unsigned)(v >> 32) != e) {
+                    if (xq4d::global_ns() - t0 > 2000000000ull) {
+                        ok = false;
+                        break;
+                    }
+                    __nanosleep(32);
+                    v = xq4d::ld_sys_u64(in + idx);
+                }
+                if (!ok) {
+                    atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                    break;
+                }
+                if (out_f32)
+                    reinterpret_cast<uint32_t *>(y)[idx] = (uint32_t)v;
+                else
+                    reinterpret_cast<uint16_t *>(y)[idx] = (uint16_t)v;
+            }
+            // the last CTA of this launch advances the epoch: every CTA has
+            // read it by the time it counts itself here
+            __syncwarp();
+            if (lane == 0 && atomicAdd(p2p.cnt, 1u) == gridDim.x - 1) {
+                *p2p.cnt = 0u;
+                *reinterpret_cast<volatile unsigned *>(p2p.epoch) = e;
+            }
         }
         return;
     }
@@ -508,15 +571,15 @@ int sm_count_of_current_device()
     return cache[dev];
 }
 
-template <int NT, bool XH>
+template <int NT, bool XH, bool P2P>
 cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int m, void *y, int out_f32,
-                       cudaStream_t st)
+                       cudaStream_t st, const xq4_p2p_out &p2p)
 {
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, XH>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT, XH, P2P>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
@@ -539,16 +602,18 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
 #else
     cfg.numAttrs = 1;
 #endif
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, XH>, pack, n, k, nb, kc, x, m, y, out_f32);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<NT, XH, P2P>, pack, n, k, nb, kc, x, m, y, out_f32, p2p);
 }
 
 }  // namespace
 
 // m in 1..16 per launch; larger m is split into 16-token slices.
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y, int out_f32,
-                            const xq4_gemv_ws &ws, cudaStream_t st)
+                            const xq4_gemv_ws &ws, cudaStream_t st, const xq4_p2p_out *p2p)
 {
     (void)ws;
+    const xq4_p2p_out none{};
+    if (p2p && m > 16) return cudaErrorInvalidValue;  // one launch per sharded call
     static_assert(xh_offset(2) + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem, "bf16 plan too large");
     static_assert(xh_offset(1) + 64 + (size_t)kXhMaxBytes + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem / 2 - 1024,
                   "fp16 plan too large for two CTAs per SM");
@@ -560,12 +625,15 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
         const uint16_t *xs = reinterpret_cast<const uint16_t *>(x) + (size_t)t0 * k;
         void *ys = reinterpret_cast<char *>(y) + (size_t)t0 * n * ysz;
         cudaError_t e;
-        if (xh_fits(mt, kp) && (long long)xq4g_nb(n) * xq4g_kc(k) >= kXhMinChunks)
-            e = launch_one<1, true>(p, n, k, xs, mt, ys, out_f32, st);
-        else if (mt <= 8)
-            e = launch_one<1, false>(p, n, k, xs, mt, ys, out_f32, st);
+        const bool xh = xh_fits(mt, kp) && (long long)xq4g_nb(n) * xq4g_kc(k) >= kXhMinChunks;
+        if (p2p)
+            e = xh ? launch_one<1, true, true>(p, n, k, xs, mt, ys, out_f32, st, *p2p)
+                   : (mt <= 8 ? launch_one<1, false, true>(p, n, k, xs, mt, ys, out_f32, st, *p2p)
+                              : launch_one<2, false, true>(p, n, k, xs, mt, ys, out_f32, st, *p2p));
         else
-            e = launch_one<2, false>(p, n, k, xs, mt, ys, out_f32, st);
+            e = xh ? launch_one<1, true, false>(p, n, k, xs, mt, ys, out_f32, st, none)
+                   : (mt <= 8 ? launch_one<1, false, false>(p, n, k, xs, mt, ys, out_f32, st, none)
+                              : launch_one<2, false, false>(p, n, k, xs, mt, ys, out_f32, st, none));
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -13,6 +13,7 @@ static __device__ unsigned int g_xq4_fault;
 #define XQ4_FAULT_GEMV_FULL 0x1u
 #define XQ4_FAULT_GEMV_EMPTY 0x2u
 #define XQ4_FAULT_GEMM_WAIT 0x4u
+#define XQ4_FAULT_PEER_WAIT 0x8u  // a peer GPU's output words did not arrive in time
 
 namespace xq4d {
 
@@ -280,6 +281,18 @@ __device__ __forceinline__ uint64_t global_ns()
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+// 64-bit words shared with other GPUs (system scope, no ordering): one
+// aligned 64-bit access is single-copy atomic, so a reader sees a word whole.
+__device__ __forceinline__ void st_sys_u64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 // Bounded wait: false if the phase did not complete within about 2 s.  A
 // waiting thread is suspended in the barrier (up to 20 us per try) instead of

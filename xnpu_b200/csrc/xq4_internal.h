@@ -29,6 +29,25 @@ struct xq4_gemv_ws {
     int ctas;          // largest grid the partial area holds
 };
 
+// Column-sharded GEMV with the gather inside the kernel.  Every output value
+// travels to each peer as one 64-bit word in the peer's inbox: the value's
+// bits in the low half, the call's epoch in the high half.  A single aligned
+// 64-bit store is seen whole or not at all, so a word whose epoch matches is
+// complete and no fence or completion flag is needed.  Inboxes have two
+// halves used by epoch parity: no rank gets more than one call ahead of
+// another (a call ends only after the peers' words of that call arrived), so a
+// half is never rewritten while a rank still reads it.
+#define XQ4_MAX_RANKS 8
+struct xq4_p2p_out {
+    int nranks, rank;
+    int n_total;                                // rows of the full output (n x nranks)
+    int row_off;                                // this rank's first row
+    unsigned long long *inbox[XQ4_MAX_RANKS];   // rank q's inbox (peer-mapped; [rank] is local)
+    size_t half_words;                          // words per parity half (>= m x n_total)
+    unsigned *cnt;                              // local: CTAs of the current launch that are done
+    unsigned *epoch;                            // local: fused calls this rank has completed
+};
+
 struct xq4_weight {
     struct xq4_device *dev;
     int ordinal;       // device ordinal (destroy does not touch `dev`)
@@ -43,7 +62,8 @@ struct xq4_weight {
 // Kernel launchers (gemv.cu, gemm_tc.cu, dequant.cu).  All return cudaError_t
 // of the launch; arguments are validated by the callers in api.cu.
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
-                            int out_f32, const struct xq4_gemv_ws &ws, cudaStream_t st);
+                            int out_f32, const struct xq4_gemv_ws &ws, cudaStream_t st,
+                            const struct xq4_p2p_out *p2p = nullptr);
 // Workspace bytes for an n-row weight and a grid of `ctas` (partials first,
 // then nb counters), and the grid the current device runs the GEMV with.
 size_t xq4_gemv_ws_bytes(int n, int ctas);
