@@ -12,10 +12,17 @@ Gate and up are one fused "gateup" projection, as in the reference's own
 layer chain (crates/xnpu-cli/src/main.rs:2464, :2488: 4 GEMV shapes per
 layer, qkv / o / gateup / down); the weight bytes are those of the two.
 
+On one GPU the step is ONE launch of the GEMV chain kernel over the 128
+projections (xq4_chain_run; the ops are independent because each reads its
+fixed activation).  The same chain with every op waiting for the previous
+one (a real decode step's dependency order) and the 128 separate GEMV
+launches (one CUDA graph) are timed beside it (``other_step_forms_ms``).
+
 On N GPUs (torchrun, one process per GPU) the FFN gateup projection is
 column-sharded N ways, with the all-gather inside the GEMV kernel over NVLink
-peer memory (xq4_linear_sharded_fused); QKV, O and down are replicated.  The step is the same token, so scaling is
-"strong".  The line also reports the lm_head 4096->128256 (f32 logits)
+peer memory (xq4_linear_sharded_fused); QKV, O and down are replicated; the
+step is the 128 launches in one CUDA graph.  The step is the same token, so
+scaling is "strong".  The line also reports the lm_head 4096->128256 (f32 logits)
 sharded the same way.
 
 Metric: tokens/s (higher is better); GB/s of algorithmic bytes (packed codes
@@ -46,6 +53,12 @@ SHARDED = ("gateup",)  # column-sharded over ranks; the rest are replicas
 #       --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
 # (every launch of the capture; the figures repeat to within 0.01 %).
 DRAM_PER_LAUNCH = {"qkv": 14231808, "o": 9512960, "gateup": 66216960, "down": 33126912}
+# DRAM bytes (read + write) of one chain launch (the whole 32-layer step), from
+#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
+#       --clock-control none -k regex:gemv_chain --csv python bench.py --layers 4
+#       --steps 1 --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
+# (a 4-layer chain; its bytes scaled by 8 = the ratio of algorithmic bytes).
+CHAIN_DRAM_PER_STEP = None
 LMHEAD = (128256, 4096)
 
 
@@ -277,8 +290,27 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # warm-up (eager), then capture one step into a CUDA graph: 128 launches
-    # per token are too many to issue from the host at HBM speed
+    def timed(run_one, steps):
+        """Device time per step (ms, max over ranks) of `steps` calls of
+        run_one on `stream`, bracketed by barrier + synchronize."""
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(steps):
+                run_one()
+        ev1.record(stream)
+        barrier()
+        t_ms = ev0.elapsed_time(ev1) / steps
+        if world > 1:
+            tt = torch.tensor([t_ms], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t_ms = float(tt.item())
+        return t_ms
+
+    # Separate launches: warm-up (eager), then one step captured into a CUDA
+    # graph (128 launches per token are too many to issue from the host at
+    # HBM speed).
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step(sp)
@@ -291,26 +323,38 @@ def main():
             graph.replay()
     barrier()
 
-    # device-timed steps (inputs resident in HBM), graph replays
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # One GPU: the step as ONE chain launch (xq4_chain_run).  Every
+    # projection reads its fixed activation (the reference's projection-stream
+    # benchmark, main.rs:2487-2499), so the ops are independent (wait_prev =
+    # 0); the same chain with every op waiting for the previous one (the
+    # dependency order of a real decode step) is timed beside it.
+    chains = {}
+    if world == 1:
+        for wp in (0, 1):
+            chains[wp] = hal.Chain(dev, [(layer[name], xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, wp)
+                                         for layer in weights for name, n, k in SHAPES])
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    chains[wp].run(stream)
+        barrier()
+
+    # device-timed steps (inputs resident in HBM)
     with ClockSampler(local) as clk:
-        barrier()
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(args.steps):
-                graph.replay()
-        ev1.record(stream)
-        barrier()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        if world == 1:
+            ms = timed(lambda: chains[0].run(stream), args.steps)
+            per_step = 1
+        else:
+            ms = timed(graph.replay, args.steps)
     clocks = clk.summary()
     launches = per_step * args.steps
+    alt = {"separate_launches_graph_ms": timed(graph.replay, args.steps)}
+    if world == 1:
+        alt["chain_dependent_ms"] = timed(lambda: chains[1].run(stream), args.steps)
+    for c in chains.values():
+        c.destroy()
 
-    # roofline: algorithmic bytes of every GEMV launch in the timed region
-    # (per GPU) over the timed region's duration
+    # roofline: algorithmic bytes of the step's GEMVs (per GPU) over the
+    # timed region's duration
     gpu_step_bytes = 0
     for name, n, k in SHAPES:
         ns = n // world if (world > 1 and name in SHARDED) else n
@@ -359,15 +403,21 @@ def main():
                        "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world}, rows gathered by the GEMV over NVLink peer memory; qkv/o/down replicated",
                        "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
             "gbs": step_bytes * (1e3 / ms) / 1e9,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "gemv_kernel<1> (decode GEMV, m=1)",
-                         "traffic": (sum(DRAM_PER_LAUNCH[nm] for nm, _, _ in SHAPES) / len(SHAPES)
-                                     if world == 1 else None),
-                         "traffic_unit": "bytes per launch, mean over the step's projections (ncu)",
-                         "algorithmic_bytes_per_launch": gpu_step_bytes / LAYERS / len(SHAPES),
-                         "region": "all GEMV launches of the timed steps (CUDA graph replays)",
-                         "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()}},
+            "roofline": ({"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "peak_kind": peak_kind,
+                          "kernel": "gemv_chain_kernel (the step's 128 GEMVs in one launch, m=1)",
+                          "traffic": (CHAIN_DRAM_PER_STEP * LAYERS / 32 if CHAIN_DRAM_PER_STEP else None),
+                          "traffic_unit": "bytes per launch (ncu, 4-layer chain scaled by bytes to 32 layers)",
+                          "algorithmic_bytes_per_launch": gpu_step_bytes,
+                          "region": "one chain launch per step"}
+                         if world == 1 else
+                         {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "peak_kind": peak_kind,
+                          "kernel": "gemv_kernel<1> (decode GEMV, m=1)", "traffic": None,
+                          "algorithmic_bytes_per_launch": gpu_step_bytes / LAYERS / len(SHAPES),
+                          "region": "all GEMV launches of the timed steps (CUDA graph replays)"}),
+            "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()},
+            "other_step_forms_ms": alt,
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
@@ -415,8 +465,18 @@ def e2e_run(dev, weights, comm, world, args):
     hx.numpy()[:] = synth.synth_x(1, x_bytes // 2, 5).reshape(-1).view(np.uint8)
     seq = ctypes.c_uint64()
 
+    chain = None
+    if comm is None:  # one GPU: the step is one chain submit (ops independent, as the timed step)
+        chain = hal.Chain(dev, [(layer[name], xb.device_ptr() + k_off[k], yb.device_ptr() + y_off[(li, name)],
+                                 1, 0, 0) for li, layer in enumerate(weights) for name, n, k in SHAPES])
+
     def one():
         check(L.xq4_buffer_upload(xb.handle, hx.data_ptr(), 0, x_bytes))
+        if chain is not None:
+            chain.submit()
+            check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
+            check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
+            return
         for li, layer in enumerate(weights):
             for name, n, k in SHAPES:
                 if comm is not None and name in SHARDED:
@@ -443,12 +503,16 @@ def e2e_run(dev, weights, comm, world, args):
         t = torch.tensor([dt], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
+    if chain is not None:
+        chain.destroy()
     xb.destroy()
     yb.destroy()
+    path = ("xq4_buffer_upload -> xq4_chain_submit (the step's 128 GEMVs) -> xq4_wait -> xq4_buffer_download "
+            "(pinned host buffers)" if chain is not None else
+            "xq4_buffer_upload -> 128 x xq4_linear (gateup: xq4_linear_sharded_fused) -> xq4_wait -> "
+            "xq4_buffer_download (pinned host buffers)")
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
-            "ms_per_step": dt * 1e3,
-            "path": "xq4_buffer_upload -> 128 x xq4_linear (gateup: xq4_linear_sharded_fused when N > 1) -> "
-                    "xq4_wait -> xq4_buffer_download (pinned host buffers)"}
+            "ms_per_step": dt * 1e3, "path": path}
 
 
 def w4a8_run(weights, xs, stream, args):

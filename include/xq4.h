@@ -172,6 +172,38 @@ int xq4_linear(xq4_device *dev, const xq4_weight *w,
 int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev,
                    int m, int out_dtype, void *stream);
 
+/* ---------------------------------------------------------------- op chains */
+/* A prebuilt chain of GEMV ops run as ONE persistent kernel: the weights of
+ * the next op stream in while the current op finishes, so a decode step's
+ * projections pay one launch ramp and tail instead of one per op.  Replaces
+ * the reference's chained op packets built once and submitted together
+ * (chain_op, crates/xnpu-cli/src/main.rs:1611-1635; the projection stream of
+ * cmd_run_w4layer, main.rs:2487-2499).  Ops run in order; an op with
+ * wait_prev != 0 reads its x only after the previous op's y is completely
+ * written (so x may be an earlier op's output); wait_prev = 0 lets the op
+ * start while the previous one is still finishing (independent inputs).
+ * Each op: m in 1..8, out_dtype XQ4_OUT_BF16/F32, x 16-byte aligned, y
+ * aligned to its element.  The op table is copied to the device at create;
+ * the pointers must stay valid while the chain is used.  A chain runs on one
+ * stream at a time (its completion counters are per chain).  A dependency
+ * wait that runs out (2 s) sets fault bit 0x10. */
+typedef struct xq4_chain xq4_chain;
+typedef struct xq4_chain_op {
+    const xq4_weight *w;
+    const void *x_dev;
+    void *y_dev;
+    int m;
+    int out_dtype;
+    int wait_prev;
+} xq4_chain_op;
+int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out);
+int xq4_chain_destroy(xq4_chain *chain);
+/* Submit on the device queue (after everything queued before); timeline
+ * point in *seq (may be NULL), as xq4_linear. */
+int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_t *seq);
+/* Run on a caller stream (a cudaStream_t; NULL = CUDA's default stream). */
+int xq4_chain_run(const xq4_chain *chain, void *stream);
+
 /* Replaces syncobj_timeline_wait(dev, syncobj, seq, timeout_ns)
  * (crates/xnpu-hal/src/ert.rs:218) and the completed-state check
  * (ert.rs:147-151): XQ4_OK when the op at `seq` and everything queued before

@@ -1,0 +1,168 @@
+"""GPU: a chain of GEMV ops run as one persistent kernel (xq4_chain_*).
+
+Bars:
+  * every op's output is bit-identical to the same op run alone through
+    xq4_linear_raw on the bf16 path (the chain runs the same per-row-block
+    arithmetic in the same order), for the 8B decode shapes, ragged n and K
+    tails (k % 64 == 32), m = 1, 3, 8 and bf16 / f32 outputs;
+  * and within the GEMV parity bars against the oracle;
+  * an op with wait_prev reads the previous op's output written in the same
+    launch (x = y of the op before) and matches the two ops run one by one;
+  * repeated runs (the completion counters reset) and the device-queue
+    submit give the same bits; no fault bit is raised.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from xnpu_b200 import hal, lib, synth
+from xnpu_b200._lib import check
+from test_gpu_kernels import assert_parity, from_dev_bf16, import_planes, rel_metrics, to_dev_u16
+
+pytestmark = pytest.mark.gpu
+
+
+def _op_inputs(n, k, m, seed):
+    q = synth.unpack_codes_signed(synth.synth_codes(n, k, seed))
+    s = synth.synth_scales(n, k, seed)
+    x = synth.synth_x(m, k, seed + 1)
+    return q, s, x
+
+
+def _raw(w, xd, m, n, f32):
+    y = torch.empty((m, n), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
+    check(lib().xq4_linear_raw(w.handle, xd.data_ptr(), y.data_ptr(), m, 1 if f32 else 0,
+                               torch.cuda.current_stream().cuda_stream))
+    return y
+
+
+def _bits(t):
+    return t.view(torch.int32 if t.dtype == torch.float32 else torch.int16)
+
+
+# below the fp16-path threshold of the single-op GEMV (so xq4_linear_raw runs
+# the bf16 path, as the chain does)
+SHAPES = [  # (n, k, m, f32)
+    (6144, 4096, 1, False),    # qkv
+    (4096, 4096, 1, False),    # o
+    (14336, 4096, 1, False),   # gate
+    (4096, 14336, 1, False),   # down
+    (333, 160, 3, False),      # ragged rows, partial stage
+    (4100, 4128, 8, True),     # K tail (k % 64 == 32), f32 out
+    (17, 96, 8, False),        # fewer row blocks than CTAs
+    (2048, 2048, 3, True),
+]
+
+
+def test_chain_matches_single_ops(dev):
+    ws, ops, refs, oracle = [], [], [], []
+    for i, (n, k, m, f32) in enumerate(SHAPES):
+        q, s, x = _op_inputs(n, k, m, 900 + i)
+        w = import_planes(dev, q, s)
+        xd = to_dev_u16(x)
+        y = torch.full((m, n), float("nan"), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
+        ws.append((w, xd, y))
+        ops.append((w, xd.data_ptr(), y.data_ptr(), m, 1 if f32 else 0, i % 2))
+        refs.append(_raw(w, xd, m, n, f32))
+        rows = np.arange(n) if n <= 1536 else np.unique(np.concatenate([np.arange(512), np.arange(n - 512, n)]))
+        oracle.append((rows, O.gemv_q(q[rows], s[rows], x)))
+    chain = hal.Chain(dev, ops)
+    for rep in range(3):
+        for _, _, y in ws:
+            y.fill_(float("nan"))
+        if rep < 2:
+            chain.run()
+        else:
+            hal.timeline_wait(dev, chain.submit(), 10_000_000_000)
+        torch.cuda.synchronize()
+        for i, ((w, xd, y), ref) in enumerate(zip(ws, refs)):
+            assert torch.equal(_bits(y), _bits(ref)), (rep, SHAPES[i])
+    assert dev.fault() == 0
+    for (n, k, m, f32), (_, _, y), (rows, ref) in zip(SHAPES, ws, oracle):
+        if f32:
+            max_rel, mae, _ = rel_metrics(y.cpu().numpy()[:, rows], ref)
+            assert max_rel <= 1e-2 and mae <= 1e-3, ((n, k, m), max_rel, mae)
+        else:
+            assert_parity(from_dev_bf16(y)[:, rows], ref, f"chain {n}x{k} m={m}")
+    chain.destroy()
+
+
+def test_chain_dependent_ops(dev):
+    """o -> gate -> down with each op reading the previous op's output (the
+    wait_prev barrier inside the launch), against the ops run one by one."""
+    m = 2
+    dims = [(4096, 4096), (14336, 4096), (4096, 14336)]  # (n, k); k of op i = n of op i-1
+    x0 = to_dev_u16(synth.synth_x(m, 4096, 77))
+    ws, ys = [], []
+    for i, (n, k) in enumerate(dims):
+        q, s, _ = _op_inputs(n, k, 1, 950 + i)
+        ws.append(import_planes(dev, q, s))
+        ys.append(torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda"))
+    ops = []
+    for i, (w, y) in enumerate(zip(ws, ys)):
+        xp = x0.data_ptr() if i == 0 else ys[i - 1].data_ptr()
+        ops.append((w, xp, y.data_ptr(), m, 0, 1))
+    chain = hal.Chain(dev, ops)
+    # one by one: the same inputs
+    ref, xin = [], x0
+    for w, (n, k) in zip(ws, dims):
+        xin = _raw(w, xin, m, n, False)
+        ref.append(xin)
+    for rep in range(2):
+        for y in ys:
+            y.fill_(float("nan"))
+        chain.run()
+        torch.cuda.synchronize()
+        for i, (y, r) in enumerate(zip(ys, ref)):
+            assert torch.equal(_bits(y), _bits(r)), (rep, i)
+    assert dev.fault() == 0
+    chain.destroy()
+
+
+def test_chain_decode_set(dev):
+    """Four layers of the 8B decode set (qkv, o, gateup, down) with fixed
+    activations, every op after the previous (the decode step's order)."""
+    shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
+    xs = {k: to_dev_u16(synth.synth_x(1, k, 60 + k % 7)) for k in (4096, 14336)}
+    ops, outs, refs = [], [], []
+    for layer in range(4):
+        for j, (n, k) in enumerate(shapes):
+            q, s, _ = _op_inputs(n, k, 1, 1000 + 4 * layer + j)
+            w = import_planes(dev, q, s)
+            y = torch.empty((1, n), dtype=torch.bfloat16, device="cuda")
+            ops.append((w, xs[k].data_ptr(), y.data_ptr(), 1, 0, 1))
+            outs.append(y)
+            if j == 2:  # gateup: the single-op GEMV takes the fp16 path here; compare with the oracle
+                rows = np.unique(np.concatenate([np.arange(256), np.arange(n - 256, n)]))
+                x = from_dev_bf16(xs[k])
+                refs.append(("oracle", rows, O.gemv_q(q[rows], s[rows], x)))
+            else:
+                refs.append(("raw", None, _raw(w, xs[k], 1, n, False)))
+    chain = hal.Chain(dev, ops)
+    chain.run()
+    torch.cuda.synchronize()
+    for i, (y, (kind, rows, r)) in enumerate(zip(outs, refs)):
+        if kind == "raw":
+            assert torch.equal(_bits(y), _bits(r)), i
+        else:
+            assert_parity(from_dev_bf16(y)[:, rows], r, f"chain gateup op {i}")
+    assert dev.fault() == 0
+    chain.destroy()
+
+
+def test_chain_rejects_bad_ops(dev):
+    q, s, x = _op_inputs(64, 64, 1, 5)
+    w = import_planes(dev, q, s)
+    xd = to_dev_u16(x)
+    y = torch.empty((9, 64), dtype=torch.bfloat16, device="cuda")
+    for op in [(w, xd.data_ptr(), y.data_ptr(), 9, 0, 0),        # m > 8
+               (w, xd.data_ptr() + 2, y.data_ptr(), 1, 0, 0),    # x not 16-byte aligned
+               (w, xd.data_ptr(), y.data_ptr() + 2, 1, 1, 0),    # f32 y not 4-byte aligned
+               (w, xd.data_ptr(), y.data_ptr(), 1, 7, 0)]:       # unknown out_dtype
+        with pytest.raises(hal.Xq4Error):
+            hal.Chain(dev, [op])
+    h = ctypes.c_void_p()
+    assert lib().xq4_chain_create(dev.handle, None, 0, ctypes.byref(h)) != 0

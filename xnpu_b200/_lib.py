@@ -65,6 +65,13 @@ class DeviceInfo(ctypes.Structure):
     ]
 
 
+class ChainOp(ctypes.Structure):
+    _fields_ = [
+        ("w", ctypes.c_void_p), ("x_dev", ctypes.c_void_p), ("y_dev", ctypes.c_void_p),
+        ("m", ctypes.c_int), ("out_dtype", ctypes.c_int), ("wait_prev", ctypes.c_int),
+    ]
+
+
 _P = ctypes.c_void_p
 _PP = ctypes.POINTER(ctypes.c_void_p)
 _I = ctypes.c_int
@@ -92,6 +99,10 @@ SIGNATURES = {
     "xq4_dequant": (_I, [_P, _P, _P]),
     "xq4_linear": (_I, [_P, _P, _P, _SZ, _P, _SZ, _I, _I, ctypes.POINTER(ctypes.c_uint64)]),
     "xq4_linear_raw": (_I, [_P, _P, _P, _I, _I, _P]),
+    "xq4_chain_create": (_I, [_P, ctypes.POINTER(ChainOp), _I, _PP]),
+    "xq4_chain_destroy": (_I, [_P]),
+    "xq4_chain_submit": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
+    "xq4_chain_run": (_I, [_P, _P]),
     "xq4_wait": (_I, [_P, ctypes.c_uint64, ctypes.c_int64]),
     "xq4_last_seq": (ctypes.c_uint64, [_P]),
     "xq4_device_fault": (_I, [_P, ctypes.POINTER(ctypes.c_uint32)]),

@@ -383,6 +383,106 @@ extern "C" int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_de
     return launch_linear(w, x_dev, y_dev, m, out_dtype, (cudaStream_t)stream);
 }
 
+// ------------------------------------------------------------------ op chains
+struct xq4_chain {
+    xq4_device *dev;
+    int ordinal;
+    int n_ops;
+    xq4_chain_op_dev *d_ops;  // op table, then n_ops + 1 completion counters
+    unsigned *d_done;
+};
+
+extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out)
+{
+    xq4_clear_error();
+    if (!dev || !ops || !out) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    *out = nullptr;
+    if (n_ops <= 0 || n_ops > (1 << 20)) return xq4_fail(XQ4_EINVAL, "n_ops %d out of range", n_ops);
+    std::vector<xq4_chain_op_dev> tab((size_t)n_ops);
+    for (int i = 0; i < n_ops; i++) {
+        const xq4_chain_op &o = ops[i];
+        if (!o.w || !o.x_dev || !o.y_dev) return xq4_fail(XQ4_EINVAL, "op %d: NULL weight or pointer", i);
+        if (o.w->dev != dev) return xq4_fail(XQ4_EINVAL, "op %d: weight of another device", i);
+        if (o.m < 1 || o.m > 8) return xq4_fail(XQ4_EINVAL, "op %d: m must be in 1..8 (got %d)", i, o.m);
+        if (o.out_dtype != XQ4_OUT_BF16 && o.out_dtype != XQ4_OUT_F32)
+            return xq4_fail(XQ4_EINVAL, "op %d: unknown out_dtype %d", i, o.out_dtype);
+        const uintptr_t ya = o.out_dtype == XQ4_OUT_F32 ? 3 : 1;
+        if (((uintptr_t)o.x_dev & 15) || ((uintptr_t)o.y_dev & ya))
+            return xq4_fail(XQ4_EINVAL, "op %d: x must be 16-byte aligned and y aligned to its element", i);
+        xq4_chain_op_dev &d = tab[(size_t)i];
+        d.pack = o.w->d_pack;
+        d.x = o.x_dev;
+        d.y = o.y_dev;
+        d.n = o.w->n;
+        d.k = o.w->k;
+        d.nb = o.w->nb;
+        d.kc = o.w->kc;
+        d.m = o.m;
+        d.out_f32 = o.out_dtype == XQ4_OUT_F32;
+        d.wait_prev = o.wait_prev != 0;
+        d.pad = 0;
+    }
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    const size_t tab_bytes = tab.size() * sizeof(xq4_chain_op_dev);
+    const size_t done_bytes = ((size_t)n_ops + 1) * sizeof(unsigned);
+    void *mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, tab_bytes + done_bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the chain: %s", tab_bytes + done_bytes, cudaGetErrorString(e));
+    }
+    e = cudaMemcpy(mem, tab.data(), tab_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset((char *)mem + tab_bytes, 0, done_bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(mem);
+        return cuda_fail(e, "chain upload");
+    }
+    xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (xq4_chain_op_dev *)mem,
+                                                (unsigned *)((char *)mem + tab_bytes)};
+    if (!c) {
+        cudaFree(mem);
+        return xq4_fail(XQ4_ENOMEM, "host allocation");
+    }
+    *out = c;
+    return XQ4_OK;
+}
+
+extern "C" int xq4_chain_destroy(xq4_chain *chain)
+{
+    xq4_clear_error();
+    if (!chain) return XQ4_OK;
+    cudaSetDevice(chain->ordinal);
+    cudaError_t e = cudaDeviceSynchronize();  // no launch of this chain still reads the table
+    cudaFree(chain->d_ops);
+    delete chain;
+    if (e != cudaSuccess) return cuda_fail(e, "chain destroy");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
+{
+    xq4_clear_error();
+    if (!chain) return xq4_fail(XQ4_EINVAL, "NULL chain");
+    CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, (cudaStream_t)stream), "chain launch");
+    return XQ4_OK;
+}
+
+extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_t *seq)
+{
+    xq4_clear_error();
+    if (!dev || !chain) return xq4_fail(XQ4_EINVAL, "NULL argument");
+    if (chain->dev != dev) return xq4_fail(XQ4_EINVAL, "chain of another device");
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, dev->stream), "chain launch");
+    const uint64_t s = dev->last_seq + 1;
+    CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");
+    dev->last_seq = s;
+    if (seq) *seq = s;
+    return XQ4_OK;
+}
+
 static uint64_t now_ns()
 {
     timespec ts;

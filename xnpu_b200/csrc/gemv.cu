@@ -126,7 +126,7 @@ __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
 // a K tail that is not a whole chunk (k % 64 == 32); the fast path has no
 // per-chunk tests.  On the fp16 path xr points at the token's fp16 row in
 // shared memory (zero padded to whole chunks).
-template <int NT, bool SAFE, bool XH>
+template <int NT, bool SAFE, bool XH, bool COH = false>
 __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, uint32_t phase, int kc0,
                                               int kc_n, int k, const uint16_t *const (&xr)[NT],
                                               const uint32_t (&xs)[NT], uint32_t tbl, int warp, int lane,
@@ -151,7 +151,7 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                         xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::lds_v4(xs[nt] + 2 * kb)
                                                              : make_uint4(0, 0, 0, 0);
                     } else if (!SAFE || (kc < kc_n && kb < k)) {
-                        xf[c][nt][G2] = xq4d::ldg_v4(xr[nt] + kb);
+                        xf[c][nt][G2] = COH ? xq4d::ldcg_v4(xr[nt] + kb) : xq4d::ldg_v4(xr[nt] + kb);
                     } else {
                         xf[c][nt][G2] = make_uint4(0, 0, 0, 0);
                     }
@@ -557,6 +557,202 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     }
 }
 
+// ------------------------------------------------------------------ GEMV chain
+// One persistent launch over a list of GEMVs (m <= 8 each, bf16 path), the
+// B200 form of the reference's chained op submission (crates/xnpu-cli/src/
+// main.rs:1611-1635, and the projection stream of cmd_run_w4layer,
+// main.rs:2487-2499).  Same warp roles as gemv_kernel.  CTA c owns the same
+// share of every op's row blocks; the producer streams op after op through
+// one ring, so the next op's weights are already in flight while the
+// consumers finish the current one, and the per-launch ramp and tail of
+// separate kernels happen once per chain.  An op marked wait_prev reads its
+// x only after every CTA has written the previous op's y: the reducers count
+// finished CTAs per op (release), one consumer thread per CTA waits for the
+// count (acquire, bounded) and releases the other consumer warps through a
+// named barrier.  x is read through L2 (ld.global.cg): it may have been
+// written earlier in the same launch.
+constexpr int kChainStages = 4;
+constexpr int kChainBarBytes = ((2 * kChainStages + 2 * kRedBufs) * 8 + 127) & ~127;
+constexpr size_t kChainRingOff = kChainBarBytes + (size_t)kRedBufs * kConsumerWarps * 128 * 4;
+constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kStageBytes;
+static_assert(kChainRingOff % 128 == 0, "ring alignment");
+static_assert(kChainSmem <= (size_t)kMaxSmem / 2 - 1024, "two chain CTAs per SM");
+
+__device__ __forceinline__ void chain_range(int nb, int cta, int G, int &rb0, int &rb1)
+{
+    rb0 = (int)((long long)cta * nb / G);
+    rb1 = (int)((long long)(cta + 1) * nb / G);
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned *__restrict__ done)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + kChainStages;
+    uint64_t *red_full = empty + kChainStages;
+    uint64_t *red_free = red_full + kRedBufs;
+    float *red = reinterpret_cast<float *>(smem + kChainBarBytes);
+    uint8_t *ring = smem + kChainRingOff;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kChainStages; s++) {
+            xq4d::mbar_init(&full[s], 1);
+            xq4d::mbar_init(&empty[s], kConsumerWarps);
+        }
+        for (int b = 0; b < kRedBufs; b++) {
+            xq4d::mbar_init(&red_full[b], kConsumerWarps);
+            xq4d::mbar_init(&red_free[b], 1);
+        }
+        xq4d::fence_barrier_init();
+    }
+    __syncthreads();
+    xq4d::grid_dep_launch();
+
+    if (warp == kProducerWarp) {  // ------------------------------ producer
+        if (lane == 0) {
+            int slot = 0, i = 0;
+            uint32_t phase = 0;
+            bool alive = true;
+            for (int o = 0; o < n_ops && alive; o++) {
+                const xq4_chain_op_dev op = ops[o];
+                int rb0, rb1;
+                chain_range(op.nb, cta, G, rb0, rb1);
+                for (int rb = rb0; rb < rb1 && alive; rb++) {
+                    for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks, i++) {
+                        if (i >= kChainStages && !xq4d::mbar_wait(&empty[slot], phase ^ 1)) {
+                            atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_EMPTY);
+                            alive = false;
+                            break;
+                        }
+                        const int cnt = min(kStageChunks, op.kc - kc0);
+                        const uint32_t bytes = (uint32_t)cnt * XQ4G_UNIT_BYTES;
+                        xq4d::mbar_arrive_expect_tx(&full[slot], bytes);
+                        xq4d::bulk_g2s(ring + (size_t)slot * kStageBytes,
+                                       op.pack + ((size_t)rb * op.kc + kc0) * XQ4G_UNIT_BYTES, bytes, &full[slot]);
+                        if (++slot == kChainStages) {
+                            slot = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    if (warp == kReducerWarp) {  // ------------------------------ reducer
+        xq4d::grid_dep_wait();
+        int rbl = 0;
+        bool alive = true;
+        for (int o = 0; o < n_ops; o++) {
+            const xq4_chain_op_dev op = ops[o];
+            int rb0, rb1;
+            chain_range(op.nb, cta, G, rb0, rb1);
+            for (int rb = rb0; alive && rb < rb1; rb++, rbl++) {
+                const int buf = rbl % kRedBufs;
+                const uint32_t use = (uint32_t)(rbl / kRedBufs);
+                if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
+                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                    alive = false;  // still counted below, so no other CTA waits on this one
+                    break;
+                }
+                const float *rd = red + (size_t)buf * kConsumerWarps * 128;  // [warp][tok][row]
+                for (int oo = lane; oo < op.m * 16; oo += 32) {
+                    const int tok = oo >> 4, r = oo & 15;
+                    float sum = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
+                    const int row = rb * XQ4G_ROWS + r;
+                    if (row < op.n) {
+                        if (op.out_f32)
+                            reinterpret_cast<float *>(op.y)[(size_t)tok * op.n + row] = sum;
+                        else
+                            reinterpret_cast<__nv_bfloat16 *>(op.y)[(size_t)tok * op.n + row] = __float2bfloat16_rn(sum);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
+            }
+            // this CTA's rows of op o are written (the warp barrier orders
+            // every lane's stores before lane 0's release)
+            __syncwarp();
+            if (lane == 0) xq4d::red_release_gpu_add(&done[o], 1u);
+        }
+        // the last CTA out leaves the counters zeroed for the next launch
+        if (lane == 0 && atomicAdd(&done[n_ops], 1u) == (unsigned)G - 1)
+            for (int o = 0; o <= n_ops; o++) done[o] = 0u;
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    xq4d::grid_dep_wait();
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t ring_s = xq4d::smem_u32(ring);
+    const uint32_t xs[1] = {0u};
+    float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+    int slot = 0, rbl = 0;
+    uint32_t phase = 0;
+    for (int o = 0; o < n_ops; o++) {
+        const xq4_chain_op_dev op = ops[o];
+        if (op.wait_prev && o > 0) {
+            if (warp == 0 && lane == 0) {
+                const uint64_t t0 = xq4d::global_ns();
+                while (xq4d::ld_acquire_gpu_u32(&done[o - 1]) < (unsigned)G) {
+                    if (xq4d::global_ns() - t0 > 2000000000ull) {
+                        atomicOr(&g_xq4_fault, XQ4_FAULT_CHAIN_WAIT);
+                        break;
+                    }
+                }
+            }
+            xq4d::named_bar_sync(1, kConsumerThreads);
+        }
+        const uint16_t *const xr[1] = {reinterpret_cast<const uint16_t *>(op.x) + (size_t)(g < op.m ? g : 0) * op.k};
+        int rb0, rb1;
+        chain_range(op.nb, cta, G, rb0, rb1);
+        const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
+        for (int rb = rb0; rb < rb1; rb++, rbl++) {
+            for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {
+                const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
+                const bool fast = k_whole && kc0 + kStageChunks <= op.kc;
+                const bool ok =
+                    fast ? consume_stage<1, false, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
+                                                                0u, warp, lane, acc)
+                         : consume_stage<1, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
+                                                               0u, warp, lane, acc);
+                if (!ok) {
+                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                    return;
+                }
+                __syncwarp();
+                if (lane == 0) xq4d::mbar_arrive(&empty[slot]);
+                if (++slot == kChainStages) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+            }
+            // row block complete: the warp's partials to buffer rbl % kRedBufs
+            const int buf = rbl % kRedBufs;
+            const uint32_t use = (uint32_t)(rbl / kRedBufs);
+            if (use > 0 && !xq4d::mbar_wait(&red_free[buf], (use - 1) & 1)) {
+                atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                return;
+            }
+            float *r = red + (size_t)buf * kConsumerWarps * 128 + (size_t)warp * 128;
+            r[(2 * t) * 16 + g] = acc[0][0];
+            r[(2 * t + 1) * 16 + g] = acc[0][1];
+            r[(2 * t) * 16 + g + 8] = acc[0][2];
+            r[(2 * t + 1) * 16 + g + 8] = acc[0][3];
+            acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);
+        }
+    }
+}
+
 int sm_count_of_current_device()
 {
     static int cache[64] = {0};
@@ -637,6 +833,31 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+size_t xq4_gemv_chain_smem() { return kChainSmem; }
+
+cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done, cudaStream_t st)
+{
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmem);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sm_count_of_current_device() * kCtasPerSm);  // every CTA resident (the op waits need it)
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kChainSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, done);
 }
 
 size_t xq4_gemv_ws_bytes(int n, int ctas)

@@ -14,6 +14,7 @@ static __device__ unsigned int g_xq4_fault;
 #define XQ4_FAULT_GEMV_EMPTY 0x2u
 #define XQ4_FAULT_GEMM_WAIT 0x4u
 #define XQ4_FAULT_PEER_WAIT 0x8u  // a peer GPU's output words did not arrive in time
+#define XQ4_FAULT_CHAIN_WAIT 0x10u  // a chain op's wait for the previous op ran out
 
 namespace xq4d {
 
@@ -35,6 +36,27 @@ __device__ __forceinline__ uint32_t ldg_stream_u32(const void *p)
 }
 
 // Activations: small, reused by every row block, keep them cached.
+// L2-coherent 16-byte load (bypasses L1): for data another CTA of the same
+// kernel may have written.
+__device__ __forceinline__ uint4 ldcg_v4(const void *p)
+{
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned *p, unsigned v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint4 ldg_v4(const void *p)
 {
     uint4 r;

@@ -48,6 +48,17 @@ struct xq4_p2p_out {
     unsigned *epoch;                            // local: fused calls this rank has completed
 };
 
+// One op of a GEMV chain, as the chain kernel reads it (device memory).
+struct xq4_chain_op_dev {
+    const uint8_t *pack;  // XQ4G weights
+    const void *x;        // bf16 [m][k]
+    void *y;              // [m][n], bf16 or f32
+    int n, k, nb, kc;     // rows, K, row blocks, 64-K chunks
+    int m, out_f32;
+    int wait_prev;        // read x only after every CTA has written the previous op's y
+    int pad;
+};
+
 struct xq4_weight {
     struct xq4_device *dev;
     int ordinal;       // device ordinal (destroy does not touch `dev`)
@@ -68,6 +79,11 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 // then nb counters), and the grid the current device runs the GEMV with.
 size_t xq4_gemv_ws_bytes(int n, int ctas);
 int xq4_gemv_ws_ctas();
+// One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
+// n_ops + 1 zeroed counters (left zeroed at the end of the launch).
+cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, unsigned *done,
+                                  cudaStream_t st);
+size_t xq4_gemv_chain_smem();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
 cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);

@@ -220,6 +220,50 @@ class LinearOp:
         return seq.value
 
 
+class Chain:
+    """A prebuilt chain of w4 linear ops run as one persistent kernel (the
+    reference's chained op packets, built once and submitted together).
+
+    ``ops`` is a list of (weight, x_ptr, y_ptr, m, out_dtype, wait_prev) with
+    raw device pointers (ints); see xq4_chain_create."""
+
+    def __init__(self, dev, ops):
+        arr = (_lib.ChainOp * len(ops))()
+        for i, (w, xp, yp, m, od, wp) in enumerate(ops):
+            arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0)
+        h = ctypes.c_void_p()
+        check(lib().xq4_chain_create(dev.handle, arr, len(ops), ctypes.byref(h)))
+        self._h, self.dev, self.n_ops = h, dev, len(ops)
+        self._keep = [op[0] for op in ops]  # the weights outlive the chain
+
+    @property
+    def handle(self):
+        if not self._h:
+            raise ValueError("chain destroyed")
+        return self._h
+
+    def submit(self):
+        """On the device queue; returns the timeline point."""
+        seq = ctypes.c_uint64()
+        check(lib().xq4_chain_submit(self.dev.handle, self.handle, ctypes.byref(seq)))
+        return seq.value
+
+    def run(self, stream=None):
+        """On the current torch stream (or ``stream``)."""
+        check(lib().xq4_chain_run(self.handle, _torch_stream(stream)))
+
+    def destroy(self):
+        if self._h:
+            lib().xq4_chain_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
 def timeline_wait(dev, seq, timeout_ns):
     """Wait until op ``seq`` (and all before it) completed; raise on timeout."""
     check(lib().xq4_wait(dev.handle, seq, int(timeout_ns)))
