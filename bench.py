@@ -58,7 +58,7 @@ DRAM_PER_LAUNCH = {"qkv": 14231808, "o": 9512960, "gateup": 66216960, "down": 33
 #       --clock-control none -k regex:gemv_chain --csv python bench.py --layers 4
 #       --steps 1 --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
 # (a 4-layer chain; its bytes scaled by 8 = the ratio of algorithmic bytes).
-CHAIN_DRAM_PER_STEP = None
+CHAIN_DRAM_PER_STEP = 3929139200
 LMHEAD = (128256, 4096)
 
 
