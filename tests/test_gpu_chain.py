@@ -1,13 +1,14 @@
 """GPU: a chain of GEMV ops run as one persistent kernel (xq4_chain_*).
 
-Bars:
-  * every op's output is bit-identical to the same op run alone through
-    xq4_linear_raw on the bf16 path (the chain runs the same per-row-block
-    arithmetic in the same order), for the 8B decode shapes, ragged n and K
-    tails (k % 64 == 32), m = 1, 3, 8 and bf16 / f32 outputs;
-  * and within the GEMV parity bars against the oracle;
-  * an op with wait_prev reads the previous op's output written in the same
-    launch (x = y of the op before) and matches the two ops run one by one;
+An op whose activation no op of the chain writes runs the fp16 path from an
+image prepared once per run; an op that reads an earlier op's output runs
+the bf16 path.  Bars:
+  * fp16-path ops: within the GEMV parity bars against the oracle (8B decode
+    shapes, ragged n and K tails with k % 64 == 32, m = 1, 3, 8, bf16 / f32
+    outputs), and bit-identical to the single-op GEMV where that one also
+    takes its fp16 path (large matrices, m <= 5 at k = 4096);
+  * bf16-path ops (wait_prev, x = the previous op's y written in the same
+    launch): bit-identical to the single-op GEMV run on the same input;
   * repeated runs (the completion counters reset) and the device-queue
     submit give the same bits; no fault bit is raised.
 """
@@ -43,8 +44,6 @@ def _bits(t):
     return t.view(torch.int32 if t.dtype == torch.float32 else torch.int16)
 
 
-# below the fp16-path threshold of the single-op GEMV (so xq4_linear_raw runs
-# the bf16 path, as the chain does)
 SHAPES = [  # (n, k, m, f32)
     (6144, 4096, 1, False),    # qkv
     (4096, 4096, 1, False),    # o
@@ -54,7 +53,16 @@ SHAPES = [  # (n, k, m, f32)
     (4100, 4128, 8, True),     # K tail (k % 64 == 32), f32 out
     (17, 96, 8, False),        # fewer row blocks than CTAs
     (2048, 2048, 3, True),
+    (28672, 4096, 3, True),    # the single-op GEMV's fp16 path too: bit-identical
+    (28672, 4096, 1, False),
 ]
+RAW_FP16 = {8, 9}  # indices where xq4_linear_raw also runs the fp16 path
+
+
+def _oracle_rows(n):
+    if n <= 1536:
+        return np.arange(n)
+    return np.unique(np.concatenate([np.arange(512), np.arange(n - 512, n)]))
 
 
 def test_chain_matches_single_ops(dev):
@@ -66,10 +74,11 @@ def test_chain_matches_single_ops(dev):
         y = torch.full((m, n), float("nan"), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
         ws.append((w, xd, y))
         ops.append((w, xd.data_ptr(), y.data_ptr(), m, 1 if f32 else 0, i % 2))
-        refs.append(_raw(w, xd, m, n, f32))
-        rows = np.arange(n) if n <= 1536 else np.unique(np.concatenate([np.arange(512), np.arange(n - 512, n)]))
+        refs.append(_raw(w, xd, m, n, f32) if i in RAW_FP16 else None)
+        rows = _oracle_rows(n)
         oracle.append((rows, O.gemv_q(q[rows], s[rows], x)))
     chain = hal.Chain(dev, ops)
+    first = None
     for rep in range(3):
         for _, _, y in ws:
             y.fill_(float("nan"))
@@ -78,8 +87,14 @@ def test_chain_matches_single_ops(dev):
         else:
             hal.timeline_wait(dev, chain.submit(), 10_000_000_000)
         torch.cuda.synchronize()
+        bits = [_bits(y).clone() for _, _, y in ws]
+        if first is None:
+            first = bits
+        for i, (b, f) in enumerate(zip(bits, first)):
+            assert torch.equal(b, f), (rep, SHAPES[i], "runs differ")
         for i, ((w, xd, y), ref) in enumerate(zip(ws, refs)):
-            assert torch.equal(_bits(y), _bits(ref)), (rep, SHAPES[i])
+            if ref is not None:
+                assert torch.equal(_bits(y), _bits(ref)), (rep, SHAPES[i])
     assert dev.fault() == 0
     for (n, k, m, f32), (_, _, y), (rows, ref) in zip(SHAPES, ws, oracle):
         if f32:
@@ -92,13 +107,17 @@ def test_chain_matches_single_ops(dev):
 
 def test_chain_dependent_ops(dev):
     """o -> gate -> down with each op reading the previous op's output (the
-    wait_prev barrier inside the launch), against the ops run one by one."""
+    wait_prev barrier inside the launch): the first op (external x, fp16
+    path) against the oracle, the others (bf16 path) bit-identical to the
+    single-op GEMV on the chain's own upstream output."""
     m = 2
     dims = [(4096, 4096), (14336, 4096), (4096, 14336)]  # (n, k); k of op i = n of op i-1
-    x0 = to_dev_u16(synth.synth_x(m, 4096, 77))
-    ws, ys = [], []
+    x0h = synth.synth_x(m, 4096, 77)
+    x0 = to_dev_u16(x0h)
+    ws, ys, qs = [], [], []
     for i, (n, k) in enumerate(dims):
         q, s, _ = _op_inputs(n, k, 1, 950 + i)
+        qs.append((q, s))
         ws.append(import_planes(dev, q, s))
         ys.append(torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda"))
     ops = []
@@ -106,27 +125,29 @@ def test_chain_dependent_ops(dev):
         xp = x0.data_ptr() if i == 0 else ys[i - 1].data_ptr()
         ops.append((w, xp, y.data_ptr(), m, 0, 1))
     chain = hal.Chain(dev, ops)
-    # one by one: the same inputs
-    ref, xin = [], x0
-    for w, (n, k) in zip(ws, dims):
-        xin = _raw(w, xin, m, n, False)
-        ref.append(xin)
     for rep in range(2):
         for y in ys:
             y.fill_(float("nan"))
         chain.run()
         torch.cuda.synchronize()
-        for i, (y, r) in enumerate(zip(ys, ref)):
-            assert torch.equal(_bits(y), _bits(r)), (rep, i)
+        rows = _oracle_rows(dims[0][0])
+        q, s = qs[0]
+        assert_parity(from_dev_bf16(ys[0])[:, rows], O.gemv_q(q[rows], s[rows], x0h), f"rep {rep} op 0")
+        for i in (1, 2):
+            ref = _raw(ws[i], ys[i - 1], m, dims[i][0], False)
+            assert torch.equal(_bits(ys[i]), _bits(ref)), (rep, i)
     assert dev.fault() == 0
     chain.destroy()
 
 
 def test_chain_decode_set(dev):
     """Four layers of the 8B decode set (qkv, o, gateup, down) with fixed
-    activations, every op after the previous (the decode step's order)."""
+    activations, every op after the previous (the decode step's order): the
+    gateups bit-identical to the single-op fp16 path, the rest against the
+    oracle."""
     shapes = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
-    xs = {k: to_dev_u16(synth.synth_x(1, k, 60 + k % 7)) for k in (4096, 14336)}
+    xh = {k: synth.synth_x(1, k, 60 + k % 7) for k in (4096, 14336)}
+    xs = {k: to_dev_u16(v) for k, v in xh.items()}
     ops, outs, refs = [], [], []
     for layer in range(4):
         for j, (n, k) in enumerate(shapes):
@@ -135,12 +156,11 @@ def test_chain_decode_set(dev):
             y = torch.empty((1, n), dtype=torch.bfloat16, device="cuda")
             ops.append((w, xs[k].data_ptr(), y.data_ptr(), 1, 0, 1))
             outs.append(y)
-            if j == 2:  # gateup: the single-op GEMV takes the fp16 path here; compare with the oracle
-                rows = np.unique(np.concatenate([np.arange(256), np.arange(n - 256, n)]))
-                x = from_dev_bf16(xs[k])
-                refs.append(("oracle", rows, O.gemv_q(q[rows], s[rows], x)))
-            else:
+            if j == 2:
                 refs.append(("raw", None, _raw(w, xs[k], 1, n, False)))
+            else:
+                rows = np.unique(np.concatenate([np.arange(256), np.arange(n - 256, n)]))
+                refs.append(("oracle", rows, O.gemv_q(q[rows], s[rows], xh[k])))
     chain = hal.Chain(dev, ops)
     chain.run()
     torch.cuda.synchronize()
@@ -148,7 +168,7 @@ def test_chain_decode_set(dev):
         if kind == "raw":
             assert torch.equal(_bits(y), _bits(r)), i
         else:
-            assert_parity(from_dev_bf16(y)[:, rows], r, f"chain gateup op {i}")
+            assert_parity(from_dev_bf16(y)[:, rows], r, f"chain op {i}")
     assert dev.fault() == 0
     chain.destroy()
 

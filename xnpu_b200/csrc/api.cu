@@ -387,9 +387,10 @@ extern "C" int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_de
 struct xq4_chain {
     xq4_device *dev;
     int ordinal;
-    int n_ops;
-    xq4_chain_op_dev *d_ops;  // op table, then n_ops + 1 completion counters
-    unsigned *d_done;
+    int n_ops, n_preps;
+    xq4_chain_op_dev *d_ops;  // one allocation: op table, n_ops + 1 completion counters,
+    unsigned *d_done;         // prep table, fp16 images
+    xq4_chain_prep_dev *d_preps;
 };
 
 extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out)
@@ -420,26 +421,89 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.m = o.m;
         d.out_f32 = o.out_dtype == XQ4_OUT_F32;
         d.wait_prev = o.wait_prev != 0;
-        d.pad = 0;
+        d.xh = 0;
+        d.xh_img = nullptr;
+        d.xh_tbl = nullptr;
+        d.xh_max = nullptr;
     }
+    // fp16 path for every op whose x no op of the chain writes: each distinct
+    // such activation is converted once per run by the prep kernel
+    struct prep_key {
+        const void *x;
+        int m, k;
+        size_t img_off, tbl_off, max_off;
+    };
+    std::vector<prep_key> preps;
+    std::vector<int> op_prep((size_t)n_ops, -1);
+    const auto align = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t tab_bytes = align(tab.size() * sizeof(xq4_chain_op_dev));
+    const size_t done_bytes = align(((size_t)n_ops + 1) * sizeof(unsigned));
+    size_t img_bytes = 0;
+    for (int i = 0; i < n_ops; i++) {
+        const xq4_chain_op &o = ops[i];
+        const char *x0 = (const char *)o.x_dev, *x1 = x0 + (size_t)o.m * o.w->k * 2;
+        bool written = false;
+        for (int j = 0; j < n_ops && !written; j++) {
+            const char *y0 = (const char *)ops[j].y_dev;
+            const char *y1 = y0 + (size_t)ops[j].m * ops[j].w->n * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
+            written = x0 < y1 && y0 < x1;
+        }
+        if (written) continue;
+        int pi = -1;
+        for (size_t q = 0; q < preps.size(); q++)
+            if (preps[q].x == o.x_dev && preps[q].m == o.m && preps[q].k == o.w->k) pi = (int)q;
+        if (pi < 0) {
+            prep_key pk{o.x_dev, o.m, o.w->k, 0, 0, 0};
+            const size_t kp = (size_t)o.w->kc * XQ4G_KCHUNK;
+            pk.img_off = img_bytes;
+            img_bytes += align((size_t)o.m * kp * 2);
+            pk.tbl_off = img_bytes;
+            img_bytes += align((size_t)o.w->kc * 16 * sizeof(float));
+            pk.max_off = img_bytes;
+            img_bytes += 256;
+            pi = (int)preps.size();
+            preps.push_back(pk);
+        }
+        op_prep[(size_t)i] = pi;
+    }
+    const size_t prep_bytes = align(preps.size() * sizeof(xq4_chain_prep_dev));
+    const size_t total = tab_bytes + done_bytes + prep_bytes + img_bytes;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
-    const size_t tab_bytes = tab.size() * sizeof(xq4_chain_op_dev);
-    const size_t done_bytes = ((size_t)n_ops + 1) * sizeof(unsigned);
     void *mem = nullptr;
-    cudaError_t e = cudaMalloc(&mem, tab_bytes + done_bytes);
+    cudaError_t e = cudaMalloc(&mem, total);
     if (e != cudaSuccess) {
         cudaGetLastError();
-        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the chain: %s", tab_bytes + done_bytes, cudaGetErrorString(e));
+        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the chain: %s", total, cudaGetErrorString(e));
     }
-    e = cudaMemcpy(mem, tab.data(), tab_bytes, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemset((char *)mem + tab_bytes, 0, done_bytes);
+    char *base = (char *)mem, *img = base + tab_bytes + done_bytes + prep_bytes;
+    std::vector<xq4_chain_prep_dev> ptab(preps.size());
+    for (size_t q = 0; q < preps.size(); q++) {
+        const prep_key &pk = preps[q];
+        ptab[q] = xq4_chain_prep_dev{pk.x, (uint16_t *)(img + pk.img_off), (float *)(img + pk.tbl_off),
+                                     (unsigned *)(img + pk.max_off), pk.m, pk.k, (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK, 0};
+    }
+    for (int i = 0; i < n_ops; i++) {
+        const int pi = op_prep[(size_t)i];
+        if (pi < 0) continue;
+        xq4_chain_op_dev &d = tab[(size_t)i];
+        d.xh = 1;
+        d.xh_img = ptab[(size_t)pi].img;
+        d.xh_tbl = (const float4 *)ptab[(size_t)pi].tbl;
+        d.xh_max = ptab[(size_t)pi].max;
+    }
+    e = cudaMemcpy(base, tab.data(), tab.size() * sizeof(xq4_chain_op_dev), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(base + tab_bytes, 0, done_bytes);
+    if (e == cudaSuccess && !ptab.empty())
+        e = cudaMemcpy(base + tab_bytes + done_bytes, ptab.data(), ptab.size() * sizeof(xq4_chain_prep_dev),
+                       cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(mem);
         return cuda_fail(e, "chain upload");
     }
-    xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (xq4_chain_op_dev *)mem,
-                                                (unsigned *)((char *)mem + tab_bytes)};
+    xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
+                                                (unsigned *)(base + tab_bytes),
+                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes)};
     if (!c) {
         cudaFree(mem);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -465,7 +529,9 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
     xq4_clear_error();
     if (!chain) return xq4_fail(XQ4_EINVAL, "NULL chain");
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, (cudaStream_t)stream), "chain launch");
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps,
+                             (cudaStream_t)stream),
+       "chain launch");
     return XQ4_OK;
 }
 
@@ -475,7 +541,9 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
     if (!dev || !chain) return xq4_fail(XQ4_EINVAL, "NULL argument");
     if (chain->dev != dev) return xq4_fail(XQ4_EINVAL, "chain of another device");
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, dev->stream), "chain launch");
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps,
+                             dev->stream),
+       "chain launch");
     const uint64_t s = dev->last_seq + 1;
     CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");
     dev->last_seq = s;

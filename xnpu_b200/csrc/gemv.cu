@@ -126,11 +126,14 @@ __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
 // a K tail that is not a whole chunk (k % 64 == 32); the fast path has no
 // per-chunk tests.  On the fp16 path xr points at the token's fp16 row in
 // shared memory (zero padded to whole chunks).
-template <int NT, bool SAFE, bool XH, bool COH = false>
+// XG (fp16 path only): the fp16 activations and the correction table come
+// from global memory (xr = the prepared fp16 rows, tblg = the table) instead
+// of this CTA's shared-memory staging.
+template <int NT, bool SAFE, bool XH, bool COH = false, bool XG = false>
 __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, uint32_t phase, int kc0,
                                               int kc_n, int k, const uint16_t *const (&xr)[NT],
                                               const uint32_t (&xs)[NT], uint32_t tbl, int warp, int lane,
-                                              float (&acc)[NT][4])
+                                              float (&acc)[NT][4], const float4 *tblg = nullptr)
 {
     // chunks whose activation runs are held in registers at once (bounds
     // the register file for 16-token tiles)
@@ -147,7 +150,9 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
 #pragma unroll
                 for (int G2 = 0; G2 < 2; G2++) {
                     const int kb = kc * XQ4G_KCHUNK + 32 * G2 + 8 * t;
-                    if (XH) {
+                    if (XH && XG) {
+                        xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::ldg_v4(xr[nt] + kb) : make_uint4(0, 0, 0, 0);
+                    } else if (XH) {
                         xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::lds_v4(xs[nt] + 2 * kb)
                                                              : make_uint4(0, 0, 0, 0);
                     } else if (!SAFE || (kc < kc_n && kb < k)) {
@@ -163,8 +168,11 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
 #pragma unroll
             for (int c = 0; c < R; c++) {
                 const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
-                zc[c] = (!SAFE || kc < kc_n) ? xq4d::lds_f4(tbl + 16 * (kc * 4 + t))
-                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (XG)
+                    zc[c] = (!SAFE || kc < kc_n) ? xq4d::ldg_f4(tblg + kc * 4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+                else
+                    zc[c] = (!SAFE || kc < kc_n) ? xq4d::lds_f4(tbl + 16 * (kc * 4 + t))
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
         uint4 cw[R];
@@ -584,6 +592,72 @@ __device__ __forceinline__ void chain_range(int nb, int cta, int G, int &rb0, in
     rb1 = (int)((long long)(cta + 1) * nb / G);
 }
 
+// Prep for the chain's fp16 path: one CTA per activation converts it as the
+// single-op GEMV's fp16 staging does (the same per-token power of two, the
+// same conversions and the same order of the group sums, so the outputs are
+// bit-identical to that path), into global memory.
+constexpr int kPrepThreads = 256;
+
+__global__ void __launch_bounds__(kPrepThreads)
+chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
+{
+    // let the chain launch now (its producers stream weights meanwhile; its
+    // consumers wait for this grid); x may come from the preceding kernel
+    xq4d::grid_dep_launch();
+    xq4d::grid_dep_wait();
+    const xq4_chain_prep_dev p = preps[blockIdx.x];
+    const uint16_t *x = reinterpret_cast<const uint16_t *>(p.x);
+    const int kp = p.kc * XQ4G_KCHUNK, runs = p.k / 8, total_runs = p.m * runs;
+    __shared__ unsigned smax[8];
+    if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
+    for (int i = threadIdx.x; i < p.kc * 16; i += kPrepThreads) p.tbl[i] = 0.f;
+    __syncthreads();
+    for (int r = threadIdx.x; r < total_runs; r += kPrepThreads) {
+        const uint4 v = xq4d::ldcg_v4(x + 8 * (size_t)r);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        unsigned mx = 0;
+#pragma unroll
+        for (int h = 0; h < 4; h++) mx = max(mx, max(w[h] & 0x7FFFu, (w[h] >> 16) & 0x7FFFu));
+        if (mx) atomicMax(&smax[r / runs], mx);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    for (int base = 0; base < total_runs; base += kPrepThreads) {  // uniform trip count: shuffles below
+        const int r = base + threadIdx.x;
+        float part = 0.f;
+        int tok = 0, kk = 0;
+        if (r < total_runs) {
+            tok = r / runs;
+            kk = 8 * (r - tok * runs);
+            float f1, f2;
+            pow2_split(tok_exponent(smax[tok]), f1, f2);
+            const uint4 v = xq4d::ldcg_v4(x + 8 * (size_t)r);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t h2[4];
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float lo = __uint_as_float(w[h] << 16) * f1 * f2;
+                const float hi = __uint_as_float(w[h] & 0xFFFF0000u) * f1 * f2;
+                const __half2 hp = __floats2half2_rn(lo, hi);
+                h2[h] = *reinterpret_cast<const uint32_t *>(&hp);
+                const float2 pf = __half22float2(hp);
+                part += pf.x + pf.y;
+            }
+            *reinterpret_cast<uint4 *>(p.img + (size_t)tok * kp + kk) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        if (r < total_runs && (lane & 3) == 0) {
+            const int grp = kk >> 5;  // group index along K
+            p.tbl[((grp >> 1) * 4 + (tok >> 1)) * 4 + (grp & 1) * 2 + (tok & 1)] = -8.f * 0x1p-24f * part;
+        }
+    }
+    const int pad_runs = (kp - p.k) / 8;  // k % 64 == 32: one half chunk per token
+    for (int i = threadIdx.x; i < p.m * pad_runs; i += kPrepThreads)
+        *reinterpret_cast<uint4 *>(p.img + (size_t)(i / pad_runs) * kp + p.k + 8 * (i % pad_runs)) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < 8) p.max[threadIdx.x] = smax[threadIdx.x];
+}
+
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned *__restrict__ done)
 {
@@ -668,6 +742,11 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                     for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
                     const int row = rb * XQ4G_ROWS + r;
                     if (row < op.n) {
+                        if (op.xh) {  // undo 2^-24 and the token's power of two (exact)
+                            float f1, f2;
+                            pow2_split(24 - tok_exponent(op.xh_max[tok]), f1, f2);
+                            sum = sum * f1 * f2;
+                        }
                         if (op.out_f32)
                             reinterpret_cast<float *>(op.y)[(size_t)tok * op.n + row] = sum;
                         else
@@ -710,19 +789,28 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
             }
             xq4d::named_bar_sync(1, kConsumerThreads);
         }
-        const uint16_t *const xr[1] = {reinterpret_cast<const uint16_t *>(op.x) + (size_t)(g < op.m ? g : 0) * op.k};
+        const int tok = g < op.m ? g : 0;
+        const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
+                                             : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
         int rb0, rb1;
         chain_range(op.nb, cta, G, rb0, rb1);
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
         for (int rb = rb0; rb < rb1; rb++, rbl++) {
             for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {
                 const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
-                const bool fast = k_whole && kc0 + kStageChunks <= op.kc;
-                const bool ok =
-                    fast ? consume_stage<1, false, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
-                                                                0u, warp, lane, acc)
-                         : consume_stage<1, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
-                                                               0u, warp, lane, acc);
+                const bool whole = kc0 + kStageChunks <= op.kc;
+                bool ok;
+                if (op.xh)  // fp16 path: K padding is zero in the image
+                    ok = whole ? consume_stage<1, false, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k,
+                                                                           xr, xs, 0u, warp, lane, acc, op.xh_tbl)
+                               : consume_stage<1, true, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k,
+                                                                          xr, xs, 0u, warp, lane, acc, op.xh_tbl);
+                else
+                    ok = (k_whole && whole)
+                             ? consume_stage<1, false, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
+                                                                    0u, warp, lane, acc)
+                             : consume_stage<1, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k, xr, xs,
+                                                                   0u, warp, lane, acc);
                 if (!ok) {
                     atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
                     return;
@@ -837,8 +925,22 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 
 size_t xq4_gemv_chain_smem() { return kChainSmem; }
 
-cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done, cudaStream_t st)
+cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done,
+                                  const xq4_chain_prep_dev *preps, int n_preps, cudaStream_t st)
 {
+    if (n_preps > 0) {  // the fp16 images first; the chain's producers start meanwhile (PDL)
+        cudaLaunchConfig_t pc = {};
+        pc.gridDim = dim3(n_preps);
+        pc.blockDim = dim3(kPrepThreads);
+        pc.stream = st;
+        cudaLaunchAttribute pa[1];
+        pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pa[0].val.programmaticStreamSerializationAllowed = 1;
+        pc.attrs = pa;
+        pc.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&pc, chain_prep_kernel, preps);
+        if (e != cudaSuccess) return e;
+    }
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);

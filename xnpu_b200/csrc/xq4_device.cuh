@@ -36,6 +36,14 @@ __device__ __forceinline__ uint32_t ldg_stream_u32(const void *p)
 }
 
 // Activations: small, reused by every row block, keep them cached.
+__device__ __forceinline__ float4 ldg_f4(const float4 *p)
+{
+    float4 r;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
 // L2-coherent 16-byte load (bypasses L1): for data another CTA of the same
 // kernel may have written.
 __device__ __forceinline__ uint4 ldcg_v4(const void *p)

@@ -56,7 +56,20 @@ struct xq4_chain_op_dev {
     int n, k, nb, kc;     // rows, K, row blocks, 64-K chunks
     int m, out_f32;
     int wait_prev;        // read x only after every CTA has written the previous op's y
-    int pad;
+    int xh;               // x comes from a prepared fp16 image (below) instead of x
+    const uint16_t *xh_img;    // [m][kc*64] fp16, x scaled by a per-token power of two
+    const float4 *xh_tbl;      // [kc][4] zero-point corrections
+    const unsigned *xh_max;    // [8] per-token max |x| (bf16 magnitude bits)
+};
+
+// One activation the chain reads through the fp16 path, converted once per
+// run (before the chain's consumers start) by the prep kernel.
+struct xq4_chain_prep_dev {
+    const void *x;        // bf16 [m][k]
+    uint16_t *img;
+    float *tbl;
+    unsigned *max;
+    int m, k, kc, pad;
 };
 
 struct xq4_weight {
@@ -82,7 +95,7 @@ int xq4_gemv_ws_ctas();
 // One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
 // n_ops + 1 zeroed counters (left zeroed at the end of the launch).
 cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, unsigned *done,
-                                  cudaStream_t st);
+                                  const struct xq4_chain_prep_dev *preps, int n_preps, cudaStream_t st);
 size_t xq4_gemv_chain_smem();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
