@@ -425,6 +425,20 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh_img = nullptr;
         d.xh_tbl = nullptr;
         d.xh_max = nullptr;
+        d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
+        d.pad2 = 0;
+    }
+    // segments: a new one starts at op 0 and at every op that waits
+    for (int i = 0; i < n_ops;) {
+        int j = i + 1;
+        while (j < n_ops && !tab[(size_t)j].wait_prev) j++;
+        long long units = 0;
+        for (int q = i; q < j; q++) {
+            tab[(size_t)q].seg_start = units;
+            units += (long long)tab[(size_t)q].nb * tab[(size_t)q].spr;
+        }
+        for (int q = i; q < j; q++) tab[(size_t)q].seg_units = units;
+        i = j;
     }
     // fp16 path for every op whose x no op of the chain writes: each distinct
     // such activation is converted once per run by the prep kernel

@@ -61,7 +61,8 @@
 namespace {
 
 // Tuning (measured on B200, see the header): 2 CTAs per SM, each with 8
-// consumer warps and a 3-stage ring of 32-chunk (18 KB) stages.
+// consumer warps and a 3-stage ring of 32-chunk (18 KB) stages (4 in the
+// chain kernel).  3 CTAs per SM cap the registers at 64 and spill.
 #ifndef XQ4_GEMV_STAGES
 #define XQ4_GEMV_STAGES 3
 #endif
@@ -74,6 +75,14 @@ namespace {
 constexpr int kConsumerWarps = XQ4_GEMV_WARPS;
 constexpr int kStageChunks = XQ4_GEMV_STAGE_CHUNKS;  // chunks per ring stage (576 B each)
 constexpr int kCpw = kStageChunks / kConsumerWarps;  // chunks per consumer warp per stage
+#ifndef XQ4_GEMV_CHUNKS_IN_FLIGHT
+#define XQ4_GEMV_CHUNKS_IN_FLIGHT 2
+#endif
+// chunks whose operands a single-token consumer warp holds in registers at
+// once (measured on B200, m = 1: 1 and 2 are equal and 7 % faster than 4,
+// which delays the first MMA of a stage behind more loads)
+constexpr int kChunksInFlight = XQ4_GEMV_CHUNKS_IN_FLIGHT;
+static_assert(kCpw % kChunksInFlight == 0, "chunks in flight must divide a warp's chunks per stage");
 constexpr int kStages = XQ4_GEMV_STAGES;
 #ifndef XQ4_GEMV_CTAS_PER_SM
 #define XQ4_GEMV_CTAS_PER_SM 2
@@ -137,7 +146,7 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
 {
     // chunks whose activation runs are held in registers at once (bounds
     // the register file for 16-token tiles)
-    constexpr int R = NT == 1 ? kCpw : 2;
+    constexpr int R = NT == 1 ? kChunksInFlight : 2;
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int c0 = 0; c0 < kCpw; c0 += R) {
@@ -579,17 +588,30 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 // count (acquire, bounded) and releases the other consumer warps through a
 // named barrier.  x is read through L2 (ld.global.cg): it may have been
 // written earlier in the same launch.
-constexpr int kChainStages = 4;
+#ifndef XQ4_CHAIN_STAGES
+#define XQ4_CHAIN_STAGES 4
+#endif
+constexpr int kChainStages = XQ4_CHAIN_STAGES;
+static_assert(kStageChunks == XQ4_GEMV_STAGE_CHUNKS_ABI, "the host splits chain work in these stages");
 constexpr int kChainBarBytes = ((2 * kChainStages + 2 * kRedBufs) * 8 + 127) & ~127;
 constexpr size_t kChainRingOff = kChainBarBytes + (size_t)kRedBufs * kConsumerWarps * 128 * 4;
 constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kStageBytes;
 static_assert(kChainRingOff % 128 == 0, "ring alignment");
-static_assert(kChainSmem <= (size_t)kMaxSmem / 2 - 1024, "two chain CTAs per SM");
+static_assert((kChainSmem + 1024) * kCtasPerSm <= 228 * 1024, "kCtasPerSm chain CTAs per SM");
 
-__device__ __forceinline__ void chain_range(int nb, int cta, int G, int &rb0, int &rb1)
+// This CTA's row blocks of op `op`: those whose first stage falls in the
+// CTA's share [cta*U/G, (cta+1)*U/G) of its segment's U stages.
+__device__ __forceinline__ void chain_range(const xq4_chain_op_dev &op, int cta, int G, int &rb0, int &rb1)
 {
-    rb0 = (int)((long long)cta * nb / G);
-    rb1 = (int)((long long)(cta + 1) * nb / G);
+    const long long lo = (long long)cta * op.seg_units / G - op.seg_start;
+    const long long hi = (long long)(cta + 1) * op.seg_units / G - op.seg_start;
+    const auto first_at = [&](long long s) -> int {  // first row block starting at stage >= s
+        if (s <= 0) return 0;
+        const long long r = (s + op.spr - 1) / op.spr;
+        return r < op.nb ? (int)r : op.nb;
+    };
+    rb0 = first_at(lo);
+    rb1 = first_at(hi);
 }
 
 // Prep for the chain's fp16 path: one CTA per activation converts it as the
@@ -694,7 +716,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
             for (int o = 0; o < n_ops && alive; o++) {
                 const xq4_chain_op_dev op = ops[o];
                 int rb0, rb1;
-                chain_range(op.nb, cta, G, rb0, rb1);
+                chain_range(op, cta, G, rb0, rb1);
                 for (int rb = rb0; rb < rb1 && alive; rb++) {
                     for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks, i++) {
                         if (i >= kChainStages && !xq4d::mbar_wait(&empty[slot], phase ^ 1)) {
@@ -725,7 +747,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
         for (int o = 0; o < n_ops; o++) {
             const xq4_chain_op_dev op = ops[o];
             int rb0, rb1;
-            chain_range(op.nb, cta, G, rb0, rb1);
+            chain_range(op, cta, G, rb0, rb1);
             for (int rb = rb0; alive && rb < rb1; rb++, rbl++) {
                 const int buf = rbl % kRedBufs;
                 const uint32_t use = (uint32_t)(rbl / kRedBufs);
@@ -793,7 +815,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
                                              : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
         int rb0, rb1;
-        chain_range(op.nb, cta, G, rb0, rb1);
+        chain_range(op, cta, G, rb0, rb1);
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
         for (int rb = rb0; rb < rb1; rb++, rbl++) {
             for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {

@@ -48,6 +48,9 @@ struct xq4_p2p_out {
     unsigned *epoch;                            // local: fused calls this rank has completed
 };
 
+// 64-K chunks per ring stage of the GEMV kernels (gemv.cu checks it).
+#define XQ4_GEMV_STAGE_CHUNKS_ABI 32
+
 // One op of a GEMV chain, as the chain kernel reads it (device memory).
 struct xq4_chain_op_dev {
     const uint8_t *pack;  // XQ4G weights
@@ -60,6 +63,13 @@ struct xq4_chain_op_dev {
     const uint16_t *xh_img;    // [m][kc*64] fp16, x scaled by a per-token power of two
     const float4 *xh_tbl;      // [kc][4] zero-point corrections
     const unsigned *xh_max;    // [8] per-token max |x| (bf16 magnitude bits)
+    // Work split: a segment is a run of ops of which only the first waits
+    // for its predecessor; its row blocks, weighted by ring stages, are cut
+    // into one contiguous share per CTA.
+    long long seg_start;  // stages of the segment before this op
+    long long seg_units;  // stages of the whole segment
+    int spr;              // stages per row block
+    int pad2;
 };
 
 // One activation the chain reads through the fp16 path, converted once per
