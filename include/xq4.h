@@ -195,6 +195,17 @@ typedef struct xq4_chain_op {
     int m;
     int out_dtype;
     int wait_prev;
+    /* NULL, or the communicator over which the op is column-sharded as
+     * xq4_linear_sharded_fused: w is this rank's row shard (every rank's of
+     * the same size), y_dev the full m x n_total output.  A rank's rows
+     * reach the peers' inboxes while the chain runs; each rank copies the
+     * peers' rows into y_dev before the next op that waits, or at the end
+     * of the launch.  All sharded ops of a chain use one communicator, their
+     * m x n_total summed is at most XQ4_FUSED_MAX_VALUES, and every rank
+     * creates and runs its chain (the same op shapes) together with the
+     * others: create is collective when it maps the inboxes, as the first
+     * xq4_linear_sharded_fused call. */
+    struct xq4_comm *comm;
 } xq4_chain_op;
 int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out);
 int xq4_chain_destroy(xq4_chain *chain);

@@ -69,6 +69,7 @@ class ChainOp(ctypes.Structure):
     _fields_ = [
         ("w", ctypes.c_void_p), ("x_dev", ctypes.c_void_p), ("y_dev", ctypes.c_void_p),
         ("m", ctypes.c_int), ("out_dtype", ctypes.c_int), ("wait_prev", ctypes.c_int),
+        ("comm", ctypes.c_void_p),
     ]
 
 

@@ -391,6 +391,7 @@ struct xq4_chain {
     xq4_chain_op_dev *d_ops;  // one allocation: op table, n_ops + 1 completion counters,
     unsigned *d_done;         // prep table, fp16 images
     xq4_chain_prep_dev *d_preps;
+    xq4_chain_p2p p2p;        // sharded ops' communicator (nranks 1: none)
 };
 
 extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out)
@@ -400,6 +401,18 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     *out = nullptr;
     if (n_ops <= 0 || n_ops > (1 << 20)) return xq4_fail(XQ4_EINVAL, "n_ops %d out of range", n_ops);
     std::vector<xq4_chain_op_dev> tab((size_t)n_ops);
+    xq4_comm *comm = nullptr;
+    for (int i = 0; i < n_ops; i++) {
+        if (!ops[i].comm) continue;
+        if (comm && ops[i].comm != comm) return xq4_fail(XQ4_EINVAL, "op %d: a second communicator in one chain", i);
+        comm = ops[i].comm;
+    }
+    xq4_chain_p2p p2p{};
+    p2p.nranks = 1;
+    if (comm) {  // maps the inboxes at the first use (collective)
+        if (int rc = xq4_comm_chain_p2p(comm, dev, &p2p)) return rc;
+    }
+    long long inbox_words = 0;
     for (int i = 0; i < n_ops; i++) {
         const xq4_chain_op &o = ops[i];
         if (!o.w || !o.x_dev || !o.y_dev) return xq4_fail(XQ4_EINVAL, "op %d: NULL weight or pointer", i);
@@ -426,7 +439,17 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh_tbl = nullptr;
         d.xh_max = nullptr;
         d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
-        d.pad2 = 0;
+        d.shard = o.comm && p2p.nranks > 1;
+        d.n_total = o.w->n * (d.shard ? p2p.nranks : 1);
+        d.row_off = d.shard ? o.w->n * p2p.rank : 0;
+        d.inbox_off = 0;
+        if (d.shard) {
+            d.inbox_off = inbox_words;
+            inbox_words += (long long)o.m * d.n_total;
+            if (inbox_words > (long long)XQ4_FUSED_MAX_VALUES)
+                return xq4_fail(XQ4_EINVAL, "sharded ops: m x n_total summed to %lld, above XQ4_FUSED_MAX_VALUES",
+                                inbox_words);
+        }
     }
     // segments: a new one starts at op 0 and at every op that waits
     for (int i = 0; i < n_ops;) {
@@ -459,7 +482,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         bool written = false;
         for (int j = 0; j < n_ops && !written; j++) {
             const char *y0 = (const char *)ops[j].y_dev;
-            const char *y1 = y0 + (size_t)ops[j].m * ops[j].w->n * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
+            const char *y1 = y0 + (size_t)ops[j].m * tab[(size_t)j].n_total * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
             written = x0 < y1 && y0 < x1;
         }
         if (written) continue;
@@ -517,7 +540,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     }
     xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
                                                 (unsigned *)(base + tab_bytes),
-                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes)};
+                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes), p2p};
     if (!c) {
         cudaFree(mem);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -543,7 +566,7 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
     xq4_clear_error();
     if (!chain) return xq4_fail(XQ4_EINVAL, "NULL chain");
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps,
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
                              (cudaStream_t)stream),
        "chain launch");
     return XQ4_OK;
@@ -555,7 +578,7 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
     if (!dev || !chain) return xq4_fail(XQ4_EINVAL, "NULL argument");
     if (chain->dev != dev) return xq4_fail(XQ4_EINVAL, "chain of another device");
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps,
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
                              dev->stream),
        "chain launch");
     const uint64_t s = dev->last_seq + 1;

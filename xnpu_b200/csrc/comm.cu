@@ -369,6 +369,28 @@ int setup_inbox(xq4_comm *comm)
 
 }  // namespace
 
+int xq4_comm_nranks(const xq4_comm *comm) { return comm->nranks; }
+int xq4_comm_rank(const xq4_comm *comm) { return comm->rank; }
+
+int xq4_comm_chain_p2p(xq4_comm *comm, const xq4_device *dev, xq4_chain_p2p *out)
+{
+    if (comm->dev != dev) return xq4_fail(XQ4_EINVAL, "communicator of another device");
+    if (comm->nranks > XQ4_MAX_RANKS) return xq4_fail(XQ4_ENOTSUP, "more than %d ranks", XQ4_MAX_RANKS);
+    *out = xq4_chain_p2p{};
+    out->nranks = comm->nranks;
+    out->rank = comm->rank;
+    if (comm->nranks == 1) return XQ4_OK;
+    cudaError_t e = cudaSetDevice(xq4_device_ordinal(comm->dev));
+    if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+    if (!comm->inbox.local)
+        if (int rc = setup_inbox(comm)) return rc;
+    for (int q = 0; q < comm->nranks; q++)
+        out->inbox[q] = (unsigned long long *)(comm->inbox.peer[q] + kInboxHead);
+    out->half_words = XQ4_FUSED_MAX_VALUES;
+    out->epoch = (unsigned *)(comm->inbox.local + 4);
+    return XQ4_OK;
+}
+
 extern "C" int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w, const void *x_dev, void *y_full_dev,
                                         int m, int out_dtype, void *stream)
 {

@@ -681,7 +681,8 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
 }
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned *__restrict__ done)
+gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned *__restrict__ done,
+                  const __grid_constant__ xq4_chain_p2p p2p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -742,12 +743,18 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
 
     if (warp == kReducerWarp) {  // ------------------------------ reducer
         xq4d::grid_dep_wait();
-        int rbl = 0;
+        // sharded ops: this launch's inbox epoch (the communicator's previous
+        // inbox user on this stream completed before grid_dep_wait returned)
+        const unsigned e = p2p.nranks > 1 ? *reinterpret_cast<volatile const unsigned *>(p2p.epoch) + 1u : 0u;
+        const size_t half = p2p.nranks > 1 ? (size_t)(e & 1u) * p2p.half_words : 0;
+        int rbl = 0, pend = 0;  // ops [pend, o] may hold sharded rows whose peer copies are not in y yet
         bool alive = true;
         for (int o = 0; o < n_ops; o++) {
             const xq4_chain_op_dev op = ops[o];
             int rb0, rb1;
             chain_range(op, cta, G, rb0, rb1);
+            const size_t ystride = op.shard ? (size_t)op.n_total : (size_t)op.n;
+            const int yoff = op.shard ? op.row_off : 0;
             for (int rb = rb0; alive && rb < rb1; rb++, rbl++) {
                 const int buf = rbl % kRedBufs;
                 const uint32_t use = (uint32_t)(rbl / kRedBufs);
@@ -769,23 +776,80 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                             pow2_split(24 - tok_exponent(op.xh_max[tok]), f1, f2);
                             sum = sum * f1 * f2;
                         }
-                        if (op.out_f32)
-                            reinterpret_cast<float *>(op.y)[(size_t)tok * op.n + row] = sum;
-                        else
-                            reinterpret_cast<__nv_bfloat16 *>(op.y)[(size_t)tok * op.n + row] = __float2bfloat16_rn(sum);
+                        const size_t idx = (size_t)tok * ystride + yoff + row;
+                        uint32_t bits;
+                        if (op.out_f32) {
+                            reinterpret_cast<float *>(op.y)[idx] = sum;
+                            bits = __float_as_uint(sum);
+                        } else {
+                            const __nv_bfloat16 h = __float2bfloat16_rn(sum);
+                            reinterpret_cast<__nv_bfloat16 *>(op.y)[idx] = h;
+                            bits = __bfloat16_as_ushort(h);
+                        }
+                        if (op.shard) {  // one word per peer (value bits + epoch)
+                            const unsigned long long word = ((unsigned long long)e << 32) | bits;
+                            for (int q = 0; q < p2p.nranks; q++)
+                                if (q != p2p.rank) xq4d::st_sys_u64(p2p.inbox[q] + half + op.inbox_off + idx, word);
+                        }
                     }
                 }
                 __syncwarp();
                 if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
+            }
+            // Before an op that waits for this one (or at the end), the
+            // peers' rows of this CTA's ranges of the pending sharded ops go
+            // from the inbox into y.  Each peer's CTA with this index
+            // computed them (equal shards, equal chains), and every CTA sends
+            // its words before it waits, so no wait depends on a waiting CTA.
+            if (p2p.nranks > 1 && (o + 1 == n_ops || ops[o + 1].wait_prev)) {
+                const uint64_t t0 = xq4d::global_ns();
+                bool ok = alive;
+                for (int s = pend; ok && s <= o; s++) {
+                    const xq4_chain_op_dev so = ops[s];
+                    if (!so.shard) continue;
+                    int s0, s1;
+                    chain_range(so, cta, G, s0, s1);
+                    const int r0 = s0 * XQ4G_ROWS, span = min(s1 * XQ4G_ROWS, so.n) - r0;
+                    if (span <= 0) continue;
+                    const unsigned long long *in = p2p.inbox[p2p.rank] + half + so.inbox_off;
+                    const int per_peer = so.m * span, total_w = (p2p.nranks - 1) * per_peer;
+                    for (int i = lane; ok && i < total_w; i += 32) {
+                        const int qi = i / per_peer, rem = i - qi * per_peer;
+                        const int tok = rem / span, row = r0 + (rem - tok * span);
+                        const int q = qi < p2p.rank ? qi : qi + 1;
+                        const size_t idx = (size_t)tok * so.n_total + (size_t)q * so.n + row;
+                        unsigned long long v = xq4d::ld_sys_u64(in + idx);
+                        while ((unsigned)(v >> 32) != e) {
+                            if (xq4d::global_ns() - t0 > 2000000000ull) {
+                                ok = false;
+                                break;
+                            }
+                            __nanosleep(32);
+                            v = xq4d::ld_sys_u64(in + idx);
+                        }
+                        if (!ok) {
+                            atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                            break;
+                        }
+                        if (so.out_f32)
+                            reinterpret_cast<uint32_t *>(so.y)[idx] = (uint32_t)v;
+                        else
+                            reinterpret_cast<uint16_t *>(so.y)[idx] = (uint16_t)v;
+                    }
+                }
+                pend = o + 1;
             }
             // this CTA's rows of op o are written (the warp barrier orders
             // every lane's stores before lane 0's release)
             __syncwarp();
             if (lane == 0) xq4d::red_release_gpu_add(&done[o], 1u);
         }
-        // the last CTA out leaves the counters zeroed for the next launch
-        if (lane == 0 && atomicAdd(&done[n_ops], 1u) == (unsigned)G - 1)
+        // the last CTA out leaves the counters zeroed for the next launch and
+        // advances the inbox epoch (every CTA read it before counting here)
+        if (lane == 0 && atomicAdd(&done[n_ops], 1u) == (unsigned)G - 1) {
             for (int o = 0; o <= n_ops; o++) done[o] = 0u;
+            if (p2p.nranks > 1) *reinterpret_cast<volatile unsigned *>(p2p.epoch) = e;
+        }
         return;
     }
 
@@ -948,7 +1012,8 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 size_t xq4_gemv_chain_smem() { return kChainSmem; }
 
 cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done,
-                                  const xq4_chain_prep_dev *preps, int n_preps, cudaStream_t st)
+                                  const xq4_chain_prep_dev *preps, int n_preps, const xq4_chain_p2p &p2p,
+                                  cudaStream_t st)
 {
     if (n_preps > 0) {  // the fp16 images first; the chain's producers start meanwhile (PDL)
         cudaLaunchConfig_t pc = {};
@@ -981,7 +1046,7 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, done);
+    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, done, p2p);
 }
 
 size_t xq4_gemv_ws_bytes(int n, int ctas)

@@ -69,8 +69,26 @@ struct xq4_chain_op_dev {
     long long seg_start;  // stages of the segment before this op
     long long seg_units;  // stages of the whole segment
     int spr;              // stages per row block
-    int pad2;
+    // Column-sharded op (the weight is this rank's row shard, y the full
+    // m x n_total output): rows go to the peers as inbox words.
+    int shard;
+    int n_total, row_off;
+    long long inbox_off;  // the op's first word in an inbox half
 };
+
+// The chain's communicator side (nranks == 1: no sharded op).
+struct xq4_chain_p2p {
+    int nranks, rank;
+    unsigned long long *inbox[XQ4_MAX_RANKS];  // rank q's inbox (peer-mapped; [rank] is local)
+    size_t half_words;
+    unsigned *epoch;               // the communicator's inbox epoch (shared with the fused GEMV)
+};
+struct xq4_comm;
+// Map the communicator's inboxes if not done yet (collective) and describe
+// them for a chain on `dev`.
+int xq4_comm_chain_p2p(struct xq4_comm *comm, const struct xq4_device *dev, struct xq4_chain_p2p *out);
+int xq4_comm_nranks(const struct xq4_comm *comm);
+int xq4_comm_rank(const struct xq4_comm *comm);
 
 // One activation the chain reads through the fp16 path, converted once per
 // run (before the chain's consumers start) by the prep kernel.
@@ -105,7 +123,8 @@ int xq4_gemv_ws_ctas();
 // One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
 // n_ops + 1 zeroed counters (left zeroed at the end of the launch).
 cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, unsigned *done,
-                                  const struct xq4_chain_prep_dev *preps, int n_preps, cudaStream_t st);
+                                  const struct xq4_chain_prep_dev *preps, int n_preps,
+                                  const struct xq4_chain_p2p &p2p, cudaStream_t st);
 size_t xq4_gemv_chain_smem();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);

@@ -224,13 +224,16 @@ class Chain:
     """A prebuilt chain of w4 linear ops run as one persistent kernel (the
     reference's chained op packets, built once and submitted together).
 
-    ``ops`` is a list of (weight, x_ptr, y_ptr, m, out_dtype, wait_prev) with
-    raw device pointers (ints); see xq4_chain_create."""
+    ``ops`` is a list of (weight, x_ptr, y_ptr, m, out_dtype, wait_prev[,
+    comm]) with raw device pointers (ints) and an optional communicator
+    handle for a column-sharded op; see xq4_chain_create."""
 
     def __init__(self, dev, ops):
         arr = (_lib.ChainOp * len(ops))()
-        for i, (w, xp, yp, m, od, wp) in enumerate(ops):
-            arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0)
+        for i, op in enumerate(ops):
+            w, xp, yp, m, od, wp = op[:6]
+            comm = op[6] if len(op) > 6 else None
+            arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0, getattr(comm, "value", comm))
         h = ctypes.c_void_p()
         check(lib().xq4_chain_create(dev.handle, arr, len(ops), ctypes.byref(h)))
         self._h, self.dev, self.n_ops = h, dev, len(ops)
