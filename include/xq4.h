@@ -160,7 +160,8 @@ int xq4_dequant(const xq4_weight *w, void *out_dev, void *stream);
  * crates/xnpu-hal/src/ert.rs:77-212; chain_op, crates/xnpu-cli/src/main.rs:
  * 1611-1635) and returns its timeline point in *seq (may be NULL).
  * x: bf16 [m][k] at x_off bytes into x_buf; y: [m][n] of out_dtype at y_off.
- * m <= 15 runs the decode GEMV kernel, m >= 16 the tensor-core GEMM. */
+ * m <= 24 runs the decode GEMV kernel (16 tokens per launch), m >= 25 the
+ * tensor-core GEMM. */
 int xq4_linear(xq4_device *dev, const xq4_weight *w,
                const xq4_buffer *x_buf, size_t x_off,
                xq4_buffer *y_buf, size_t y_off,

@@ -1,4 +1,4 @@
-"""GPU parity of the tcgen05 dequant-GEMM (m >= 16) through the C ABI.
+"""GPU parity of the tcgen05 dequant-GEMM (m >= 25) through the C ABI.
 
 The GEMM multiplies x by the dequantized weights RNE_bf16(q * s) (the
 reference's dequant, main.rs:3097-3125) with f32 accumulation, so its own
@@ -9,7 +9,9 @@ bit-exact on the KAT fixtures (exact arithmetic in any order); max relative
 error <= 1e-2 with the floored denominator and mean absolute error <= 1e-3 on
 seeded synthetic data (the rationale is in test_gpu_kernels.py), 5e-3 for f32
 outputs; at prefill sizes a plain torch fp32 matmul of the bit-exact
-dequantized weights covers every output.
+dequantized weights covers every output.  xq4_linear runs the GEMM from
+m = GEMM_MIN_M on; below it the GEMV (unrounded weights, the formula of
+main.rs:2287-2296), whose oracle is the unrounded-weight GEMV.
 """
 import numpy as np
 import pytest
@@ -21,6 +23,15 @@ from test_gpu_kernels import (MAE, MAX_REL, assert_parity, from_dev_bf16, import
                               row_subset, to_dev_u16)
 
 pytestmark = pytest.mark.gpu
+
+GEMM_MIN_M = 25  # xq4_linear's routing (XQ4_GEMM_MIN_M in xq4_internal.h)
+
+
+def oracle_for(q, s, x, rows, m):
+    """The oracle of the path xq4_linear takes for m tokens."""
+    if m < GEMM_MIN_M:
+        return O.gemv_q(q[rows], s[rows], x)
+    return O.gemv_bf16(O.dequant_planes(q[rows], s[rows]), x)
 
 
 def make(n, k, seed):
@@ -49,8 +60,7 @@ def test_gemm_parity_batch_sweep(dev, m):
     w = import_planes(dev, q, s)
     y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
     rows = row_subset(n, limit=768)
-    wd = O.dequant_planes(q[rows], s[rows])
-    assert_parity(y[:, rows], O.gemv_bf16(wd, x), f"m={m} (bf16 weights)")
+    assert_parity(y[:, rows], oracle_for(q, s, x, rows, m), f"m={m}")
     # Against the unrounded-weight GEMV (main.rs:2287-2296): rounding each
     # weight to bf16 moves it by at most 2^-9 relative, so the outputs may
     # differ by 2^-9 * sum|w||x| (plus both sides' final bf16 rounding and
@@ -62,8 +72,9 @@ def test_gemm_parity_batch_sweep(dev, m):
     assert np.all(np.abs(got - yq) <= 2.0 ** -9 * bound * 1.01 + 2.0 ** -8 * np.abs(yq)), f"m={m}"
 
 
-@pytest.mark.parametrize("n,k,m", [(17, 96, 16), (333, 160, 40), (4100, 4128, 33), (130, 14336, 20),
-                                   (14336, 4096, 64), (4096, 14336, 24)])
+@pytest.mark.parametrize("n,k,m", [(17, 96, 16), (17, 96, 25), (333, 160, 40), (4100, 4128, 33),
+                                   (130, 14336, 20), (130, 14336, 28), (14336, 4096, 64), (4096, 14336, 24),
+                                   (4096, 14336, 25)])
 def test_gemm_parity_ragged_and_8b_shapes(dev, n, k, m):
     """Ragged features (not a multiple of the 128-feature tile), K with a
     half chunk (k % 64 == 32), ragged token counts, and the 8B-shaped
@@ -73,7 +84,7 @@ def test_gemm_parity_ragged_and_8b_shapes(dev, n, k, m):
     w = import_planes(dev, q, s)
     y = from_dev_bf16(hal.linear(w, to_dev_u16(x)))
     rows = row_subset(n, limit=768)
-    assert_parity(y[:, rows], O.gemv_bf16(O.dequant_planes(q[rows], s[rows]), x), f"{n}x{k} m={m}")
+    assert_parity(y[:, rows], oracle_for(q, s, x, rows, m), f"{n}x{k} m={m}")
 
 
 def test_gemm_f32_output(dev):

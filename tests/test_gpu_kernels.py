@@ -188,7 +188,7 @@ def test_gemv_parity_8b_shapes(dev, name):
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 5, 8, 9, 12, 15])
 def test_gemv_parity_batch_sweep(dev, m):
-    """4096 -> 14336 gate projection, the decode batch sweep below m=16."""
+    """4096 -> 14336 gate projection, the decode batch sweep of one 16-token launch."""
     n, k = 14336, 4096
     q = synth.unpack_codes_signed(synth.synth_codes(n, k, 200))
     s = synth.synth_scales(n, k, 200)

@@ -1,7 +1,7 @@
 """Column (N) sharded linear on two GPUs.
 
 Two processes (one per GPU) import their row shard of one matrix, run the
-shard's GEMV (m < 16) or GEMM (m >= 16), all-gather the slices with NCCL
+shard's GEMV (m < 25) or GEMM (m >= 25), all-gather the slices with NCCL
 (xq4_linear_sharded) and must both hold the full output, within the parity
 bars of the single-GPU tests against the oracle over the full matrix.  For
 m < 16 the same call with the gather fused into the GEMV over peer memory
@@ -64,7 +64,7 @@ def _rank_main(rank, world, id_q, res_q):
         w = hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=rank * ns,
                                                           row_end=(rank + 1) * ns))
         rows = np.arange(0, n, 7)
-        for m, f32 in ((1, 0), (1, 1), (3, 0), (20, 0)):
+        for m, f32 in ((1, 0), (1, 1), (3, 0), (20, 0), (40, 0)):
             x = synth.synth_x(m, k, 56 + m)
             xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
             yd = torch.empty((m, n), dtype=torch.float32 if f32 else torch.bfloat16, device="cuda")
@@ -73,7 +73,7 @@ def _rank_main(rank, world, id_q, res_q):
             check(L.xq4_linear_sharded(comm, w.handle, xd.data_ptr(), yd.data_ptr(), ws.data_ptr(), m, f32, st))
             torch.cuda.synchronize()
             got = yd.float().cpu().numpy()[:, rows]
-            if m < 16:
+            if m < 25:  # the GEMV path (unrounded weights); the GEMM from m = 25
                 ref = O.gemv_q(q[rows], s[rows], x)
             else:
                 ref = O.gemv_bf16(O.dequant_planes(q[rows], s[rows]), x)

@@ -344,9 +344,10 @@ static int launch_linear(const xq4_weight *w, const void *x, void *y, int m, int
     if (((uintptr_t)x & 15) || ((uintptr_t)y & 15))
         return xq4_fail(XQ4_EINVAL, "x and y must be 16-byte aligned");
     const int f32 = out_dtype == XQ4_OUT_F32;
-    cudaError_t e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x, m, y, f32, w->ws, st)
-                           : xq4_launch_gemm(w->d_pack, w->n, w->k, x, m, y, f32, st);
-    if (e != cudaSuccess) return cuda_fail(e, m < 16 ? "gemv launch" : "gemm launch");
+    const bool gemv = xq4_use_gemv(m);
+    cudaError_t e = gemv ? xq4_launch_gemv(w->d_pack, w->n, w->k, x, m, y, f32, w->ws, st)
+                         : xq4_launch_gemm(w->d_pack, w->n, w->k, x, m, y, f32, st);
+    if (e != cudaSuccess) return cuda_fail(e, gemv ? "gemv launch" : "gemm launch");
     return XQ4_OK;
 }
 
@@ -495,7 +496,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
             pk.img_off = img_bytes;
             img_bytes += align((size_t)o.m * kp * 2);
             pk.tbl_off = img_bytes;
-            img_bytes += align((size_t)o.w->kc * 16 * sizeof(float));
+            img_bytes += align((size_t)o.w->kc * 32 * sizeof(float));
             pk.max_off = img_bytes;
             img_bytes += 256;
             pi = (int)preps.size();

@@ -180,8 +180,8 @@ extern "C" int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w, const voi
     const size_t slice = (size_t)m * ns;  // elements per rank
     char *gather = (char *)(m == 1 ? y_full_dev : ws_dev);
     void *mine = gather + (size_t)comm->rank * slice * esz;
-    e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
-               : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
+    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
+                        : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
     ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
     if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");
@@ -270,8 +270,8 @@ extern "C" int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w, c
     const size_t slice = (size_t)m * ns;  // elements per rank
     char *gather = (char *)(m == 1 ? y_full_dev : ws);
     void *mine = gather + (size_t)comm->rank * slice * esz;
-    e = m < 16 ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
-               : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
+    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
+                        : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
     ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
     if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather");

@@ -1,4 +1,4 @@
-// gemm_tc.cu -- K2: batched-decode / prefill dequant-GEMM (m >= 16) on the
+// gemm_tc.cu -- K2: batched-decode / prefill dequant-GEMM (m >= 25) on the
 // 5th-generation tensor cores (tcgen05, accumulators in tensor memory).
 //
 // y[m][n] = x[m][k] . dequant(W)^T with dequant(W) = RNE_bf16(q * scale), the

@@ -172,16 +172,21 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                 }
         }
         if (c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
-        float4 zc[R];  // fp16 path: zero-point corrections of the chunk's two groups
+        // fp16 path: zero-point corrections of the chunk's two groups; from
+        // the prepared table (XG) they are the MMA's accumulator inputs as
+        // they stand, {z(2t), z(2t+1), 16 z(2t), 16 z(2t+1)} per group
+        float4 zc[R][2];
         if (XH) {
 #pragma unroll
             for (int c = 0; c < R; c++) {
                 const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
-                if (XG)
-                    zc[c] = (!SAFE || kc < kc_n) ? xq4d::ldg_f4(tblg + kc * 4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
-                else
-                    zc[c] = (!SAFE || kc < kc_n) ? xq4d::lds_f4(tbl + 16 * (kc * 4 + t))
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                const bool in = !SAFE || kc < kc_n;
+                if (XG) {
+                    zc[c][0] = in ? xq4d::ldg_f4(tblg + (kc * 4 + t) * 2) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    zc[c][1] = in ? xq4d::ldg_f4(tblg + (kc * 4 + t) * 2 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                } else {
+                    zc[c][0] = in ? xq4d::lds_f4(tbl + 16 * (kc * 4 + t)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
         }
         uint4 cw[R];
@@ -207,8 +212,7 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                 const float s_lo = __uint_as_float(sg << 16);    // row g
                 float s_hi = __uint_as_float(sg & 0xFFFF0000u);  // row g+8
                 uint32_t a0[4], a1[4];
-                if (XH) {
-                    s_hi *= 0.0625f;  // rows g+8 carry 16*c (unpack_word_c16)
+                if (XH) {  // rows g+8 carry 16*c (unpack_word_c16): their sums are 16x until the row block ends
                     xq4d::unpack_word_c16(words[2 * G2], a0);
                     xq4d::unpack_word_c16(words[2 * G2 + 1], a1);
                 } else {
@@ -222,8 +226,19 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                         // accumulator starts at -8 * sum(x) of the group
                         // (x 2^-24; x 16 for rows g+8): the MMA then yields
                         // 2^-24 * sum((c - 8) * x) = 2^-24 * sum(q * x)
-                        const float z0 = G2 ? zc[c].z : zc[c].x, z1 = G2 ? zc[c].w : zc[c].y;
-                        const float cin[4] = {z0, z1, 16.f * z0, 16.f * z1};
+                        float cin[4];
+                        if (XG) {
+                            cin[0] = zc[c][G2].x;
+                            cin[1] = zc[c][G2].y;
+                            cin[2] = zc[c][G2].z;
+                            cin[3] = zc[c][G2].w;
+                        } else {
+                            const float z0 = G2 ? zc[c][0].z : zc[c][0].x, z1 = G2 ? zc[c][0].w : zc[c][0].y;
+                            cin[0] = z0;
+                            cin[1] = z1;
+                            cin[2] = 16.f * z0;
+                            cin[3] = 16.f * z1;
+                        }
                         xq4d::mma_f16_16816_c(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y, cin);
                         xq4d::mma_f16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
                     } else {
@@ -561,10 +576,11 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
                 float *r = rd + (size_t)warp * NT * 128 + (size_t)nt * 128;
+                const float hs = XH ? 0.0625f : 1.f;  // fp16 path: rows g+8 summed 16 * c
                 r[(2 * t) * 16 + g] = acc[nt][0];
                 r[(2 * t + 1) * 16 + g] = acc[nt][1];
-                r[(2 * t) * 16 + g + 8] = acc[nt][2];
-                r[(2 * t + 1) * 16 + g + 8] = acc[nt][3];
+                r[(2 * t) * 16 + g + 8] = acc[nt][2] * hs;
+                r[(2 * t + 1) * 16 + g + 8] = acc[nt][3] * hs;
                 acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
             }
             __syncwarp();
@@ -632,7 +648,7 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     const int kp = p.kc * XQ4G_KCHUNK, runs = p.k / 8, total_runs = p.m * runs;
     __shared__ unsigned smax[8];
     if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
-    for (int i = threadIdx.x; i < p.kc * 16; i += kPrepThreads) p.tbl[i] = 0.f;
+    for (int i = threadIdx.x; i < p.kc * 32; i += kPrepThreads) p.tbl[i] = 0.f;
     __syncthreads();
     for (int r = threadIdx.x; r < total_runs; r += kPrepThreads) {
         const uint4 v = xq4d::ldcg_v4(x + 8 * (size_t)r);
@@ -670,8 +686,12 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
         part += __shfl_xor_sync(0xffffffffu, part, 1);
         part += __shfl_xor_sync(0xffffffffu, part, 2);
         if (r < total_runs && (lane & 3) == 0) {
+            // (chunk, lane quad, group of the chunk): {z(2t), z(2t+1), 16 z(2t), 16 z(2t+1)}
             const int grp = kk >> 5;  // group index along K
-            p.tbl[((grp >> 1) * 4 + (tok >> 1)) * 4 + (grp & 1) * 2 + (tok & 1)] = -8.f * 0x1p-24f * part;
+            const float z = -8.f * 0x1p-24f * part;
+            float *e = p.tbl + (((grp >> 1) * 4 + (tok >> 1)) * 2 + (grp & 1)) * 4 + (tok & 1);
+            e[0] = z;
+            e[2] = 16.f * z;
         }
     }
     const int pad_runs = (kp - p.k) / 8;  // k % 64 == 32: one half chunk per token
@@ -916,10 +936,11 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                 return;
             }
             float *r = red + (size_t)buf * kConsumerWarps * 128 + (size_t)warp * 128;
+            const float hs = op.xh ? 0.0625f : 1.f;  // fp16 path: rows g+8 summed 16 * c
             r[(2 * t) * 16 + g] = acc[0][0];
             r[(2 * t + 1) * 16 + g] = acc[0][1];
-            r[(2 * t) * 16 + g + 8] = acc[0][2];
-            r[(2 * t + 1) * 16 + g + 8] = acc[0][3];
+            r[(2 * t) * 16 + g + 8] = acc[0][2] * hs;
+            r[(2 * t + 1) * 16 + g + 8] = acc[0][3] * hs;
             acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
             __syncwarp();
             if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);

@@ -61,7 +61,7 @@ struct xq4_chain_op_dev {
     int wait_prev;        // read x only after every CTA has written the previous op's y
     int xh;               // x comes from a prepared fp16 image (below) instead of x
     const uint16_t *xh_img;    // [m][kc*64] fp16, x scaled by a per-token power of two
-    const float4 *xh_tbl;      // [kc][4] zero-point corrections
+    const float4 *xh_tbl;      // [kc][4][2]: the zero-point MMA accumulator inputs per group
     const unsigned *xh_max;    // [8] per-token max |x| (bf16 magnitude bits)
     // Work split: a segment is a run of ops of which only the first waits
     // for its predecessor; its row blocks, weighted by ring stages, are cut
@@ -110,6 +110,15 @@ struct xq4_weight {
     void *d_ws;        // GEMV workspace allocation (xq4_gemv_ws_bytes)
     struct xq4_gemv_ws ws;
 };
+
+// Smallest m that runs the tensor-core GEMM; below it the decode GEMV (in
+// 16-token launches) streams the weights.  Measured on B200 (gate
+// 14336x4096): GEMV 19 us at m = 16 and 29 us at m = 24 against the GEMM's
+// 33 and 35 us; equal near m = 28; the GEMM is ahead from m = 32.
+#ifndef XQ4_GEMM_MIN_M
+#define XQ4_GEMM_MIN_M 25
+#endif
+static inline bool xq4_use_gemv(int m) { return m < XQ4_GEMM_MIN_M; }
 
 // Kernel launchers (gemv.cu, gemm_tc.cu, dequant.cu).  All return cudaError_t
 // of the launch; arguments are validated by the callers in api.cu.
