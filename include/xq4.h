@@ -207,6 +207,24 @@ typedef struct xq4_chain_op {
      * others: create is collective when it maps the inboxes, as the first
      * xq4_linear_sharded_fused call. */
     struct xq4_comm *comm;
+    /* Decode-step glue fused into the op (NULL / 0 = none; not with comm),
+     * each as the reference computes it (crates/xnpu-cli/src/main.rs:
+     * 4714-4745):
+     *   norm_w_dev: x is RMS-normalised per token with these k bf16 weights
+     *     before the product, RNE_bf16(x * inv * w) with inv = 1 /
+     *     sqrt(mean(x^2) + norm_eps) (rms_norm_bf16); x must be an
+     *     activation no op of the chain writes;
+     *   residual_dev: y = RNE_bf16(RNE_bf16(W x) + residual), residual bf16
+     *     [m][n] (add_bf16; it may be an earlier op's y when a wait_prev lies
+     *     between them); bf16 output only;
+     *   swiglu: the weight's rows alternate gate_i, up_i (an interleaved
+     *     gate/up projection, n even); y is bf16 [m][n/2] with
+     *     y[i] = RNE_bf16(g * (1 / (1 + exp(-g))) * u) of the op's bf16
+     *     outputs g = row 2i, u = row 2i+1 (swiglu_bf16). */
+    const void *norm_w_dev;
+    float norm_eps;
+    const void *residual_dev;
+    int swiglu;
 } xq4_chain_op;
 int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out);
 int xq4_chain_destroy(xq4_chain *chain);

@@ -43,6 +43,9 @@ _SIGS = {
     "q4o_quantize_x": (_I, [_u16p, _I, _i8p, _u16p]),
     "q4o_sum_chunk_partials": (None, [_u16p, _I, _I, _u16p]),
     "q4o_gemv_w4a8": (_I, [_i8p, _u16p, _I, _I, _i8p, _u16p, _I, _f32p, _I]),
+    "q4o_rms_norm_bf16": (None, [_u16p, _u16p, _I, ctypes.c_float, _u16p]),
+    "q4o_add_bf16": (None, [_u16p, _u16p, _SZ, _u16p]),
+    "q4o_swiglu_bf16": (None, [_u16p, _I, _u16p]),
 }
 
 
@@ -249,3 +252,34 @@ def gemv_w4a8(q, s, xq, dx, nthreads=8):
     _ok(lib().q4o_gemv_w4a8(_p(q, _i8p), _p(s, _u16p), n, k, _p(xq, _i8p), _p(dx, _u16p), m, _p(y, _f32p),
                             nthreads), "gemv_w4a8")
     return y
+
+
+def rms_norm(x, w, eps=1e-5):
+    """x: bf16 bits [m][k], w: bf16 bits [k] -> bf16 bits [m][k]
+    (crates/xnpu-cli/src/main.rs:4714-4724, per token)."""
+    x = np.ascontiguousarray(x, dtype=np.uint16).reshape(-1, np.shape(x)[-1])
+    w = np.ascontiguousarray(w, dtype=np.uint16)
+    out = np.empty_like(x)
+    for t in range(x.shape[0]):
+        lib().q4o_rms_norm_bf16(_p(x[t], _u16p), _p(w, _u16p), x.shape[1], eps, _p(out[t], _u16p))
+    return out
+
+
+def add_bf16(a, b):
+    """RNE_bf16(a + b) elementwise on bf16 bits (main.rs:4726-4730)."""
+    a = np.ascontiguousarray(a, dtype=np.uint16)
+    b = np.ascontiguousarray(b, dtype=np.uint16)
+    out = np.empty_like(a)
+    lib().q4o_add_bf16(_p(a, _u16p), _p(b, _u16p), a.size, _p(out, _u16p))
+    return out
+
+
+def swiglu(x):
+    """silu(gate) * up of fused [gate | up] bf16 rows [m][2h] -> [m][h]
+    (main.rs:4732-4745, scalar path)."""
+    x = np.ascontiguousarray(x, dtype=np.uint16).reshape(-1, np.shape(x)[-1])
+    h = x.shape[1] // 2
+    out = np.empty((x.shape[0], h), dtype=np.uint16)
+    for t in range(x.shape[0]):
+        lib().q4o_swiglu_bf16(_p(x[t], _u16p), h, _p(out[t], _u16p))
+    return out

@@ -629,3 +629,36 @@ int q4o_gemv_w4a8(const int8_t *qw, const uint16_t *sw, int n, int k, const int8
     for (int t = 0; t < started; t++) pthread_join(th[t], NULL);
     return Q4O_OK;
 }
+
+/* ------------------------------------------------------------------ decode-step glue */
+
+/* RMSNorm of one token: sequential f32 sum of squares, inv = 1 / sqrt(mean +
+ * 1e-5), out = RNE_bf16(x * inv * w).  crates/xnpu-cli/src/main.rs:4714-4724 */
+void q4o_rms_norm_bf16(const uint16_t *x, const uint16_t *w, int k, float eps, uint16_t *out)
+{
+    float sum = 0.f;
+    for (int i = 0; i < k; i++) {
+        const float v = q4o_bf16_to_f32(x[i]);
+        sum += v * v;
+    }
+    const float inv = 1.f / sqrtf(sum / (float)k + eps);
+    for (int i = 0; i < k; i++) out[i] = q4o_f32_to_bf16(q4o_bf16_to_f32(x[i]) * inv * q4o_bf16_to_f32(w[i]));
+}
+
+/* out = RNE_bf16(a + b).  crates/xnpu-cli/src/main.rs:4726-4730 */
+void q4o_add_bf16(const uint16_t *a, const uint16_t *b, size_t n, uint16_t *out)
+{
+    for (size_t i = 0; i < n; i++) out[i] = q4o_f32_to_bf16(q4o_bf16_to_f32(a[i]) + q4o_bf16_to_f32(b[i]));
+}
+
+/* silu(gate) * up over the halves of a fused [gate | up] vector of 2*half
+ * values: out[i] = RNE_bf16(g * (1 / (1 + exp(-g))) * u).
+ * crates/xnpu-cli/src/main.rs:4732-4745 (its scalar path) */
+void q4o_swiglu_bf16(const uint16_t *x, int half, uint16_t *out)
+{
+    for (int i = 0; i < half; i++) {
+        const float g = q4o_bf16_to_f32(x[i]);
+        const float u = q4o_bf16_to_f32(x[half + i]);
+        out[i] = q4o_f32_to_bf16(g * (1.f / (1.f + expf(-g))) * u);
+    }
+}

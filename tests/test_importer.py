@@ -96,6 +96,22 @@ def test_import_end_to_end(tmp_path):
                 assert (np.abs(g - y[rows]) <= 0.01 + 0.01 * np.abs(y[rows])).all(), shape
 
 
+def test_import_interleaved_gateup(tmp_path):
+    model = tmp_path / "tiny.safetensors"
+    tensors = _tiny_model(model, layers=1)
+    out = tmp_path / "w4"
+    meta = I.import_layers(model, out, log=lambda *_: None, interleave_gateup=True)
+    assert meta["gateup_rows"].startswith("interleaved")
+    g = I.bf16_bits_to_f32(tensors["model.layers.0.mlp.gate_proj.weight"][1])
+    u = I.bf16_bits_to_f32(tensors["model.layers.0.mlp.up_proj.weight"][1])
+    n, k = 2 * g.shape[0], g.shape[1]
+    q, s = O.l1_unpack(np.fromfile(out / "layer00_gateup.bin", dtype=np.uint8), n, k, 16)
+    qg, sg = I.quantize_group32(g)
+    qu, su = I.quantize_group32(u)
+    assert np.array_equal(q[0::2], qg) and np.array_equal(q[1::2], qu)
+    assert np.array_equal(s[0::2], sg) and np.array_equal(s[1::2], su)
+
+
 def test_safetensors_reader_dtypes(tmp_path):
     a = _rng(4).normal(size=(3, 5)).astype(np.float32)
     path = tmp_path / "d.safetensors"

@@ -70,6 +70,8 @@ class ChainOp(ctypes.Structure):
         ("w", ctypes.c_void_p), ("x_dev", ctypes.c_void_p), ("y_dev", ctypes.c_void_p),
         ("m", ctypes.c_int), ("out_dtype", ctypes.c_int), ("wait_prev", ctypes.c_int),
         ("comm", ctypes.c_void_p),
+        ("norm_w_dev", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("residual_dev", ctypes.c_void_p),
+        ("swiglu", ctypes.c_int),
     ]
 
 

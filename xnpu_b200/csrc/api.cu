@@ -441,6 +441,19 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh_max = nullptr;
         d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
         d.shard = o.comm && p2p.nranks > 1;
+        d.residual = (const uint16_t *)o.residual_dev;
+        d.swiglu = o.swiglu != 0;
+        d.pad3 = 0;
+        if (o.residual_dev || o.swiglu || o.norm_w_dev) {
+            if (o.comm) return xq4_fail(XQ4_EINVAL, "op %d: fused glue with a sharded op", i);
+            if ((o.residual_dev || o.swiglu) && o.out_dtype != XQ4_OUT_BF16)
+                return xq4_fail(XQ4_EINVAL, "op %d: a residual or SwiGLU epilogue writes bf16 only", i);
+            if (o.residual_dev && o.swiglu) return xq4_fail(XQ4_EINVAL, "op %d: residual and SwiGLU together", i);
+            if (o.swiglu && (o.w->n & 1)) return xq4_fail(XQ4_EINVAL, "op %d: SwiGLU needs an even row count", i);
+            if ((uintptr_t)o.residual_dev & 1) return xq4_fail(XQ4_EINVAL, "op %d: residual not 2-byte aligned", i);
+            if ((uintptr_t)o.norm_w_dev & 15) return xq4_fail(XQ4_EINVAL, "op %d: norm weights not 16-byte aligned", i);
+            if (o.norm_w_dev && !(o.norm_eps >= 0.f)) return xq4_fail(XQ4_EINVAL, "op %d: norm_eps must be >= 0", i);
+        }
         d.n_total = o.w->n * (d.shard ? p2p.nranks : 1);
         d.row_off = d.shard ? o.w->n * p2p.rank : 0;
         d.inbox_off = 0;
@@ -469,7 +482,14 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     struct prep_key {
         const void *x;
         int m, k;
+        const void *norm_w;
+        float eps;
         size_t img_off, tbl_off, max_off;
+    };
+    // bytes of op j's output
+    const auto y_bytes = [&](int j) {
+        const size_t rows = tab[(size_t)j].swiglu ? (size_t)tab[(size_t)j].n / 2 : (size_t)tab[(size_t)j].n_total;
+        return (size_t)ops[j].m * rows * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
     };
     std::vector<prep_key> preps;
     std::vector<int> op_prep((size_t)n_ops, -1);
@@ -483,15 +503,21 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         bool written = false;
         for (int j = 0; j < n_ops && !written; j++) {
             const char *y0 = (const char *)ops[j].y_dev;
-            const char *y1 = y0 + (size_t)ops[j].m * tab[(size_t)j].n_total * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
+            const char *y1 = y0 + y_bytes(j);
             written = x0 < y1 && y0 < x1;
         }
-        if (written) continue;
+        if (written) {
+            if (o.norm_w_dev)
+                return xq4_fail(XQ4_EINVAL, "op %d: RMSNorm needs an activation no op of the chain writes", i);
+            continue;
+        }
         int pi = -1;
         for (size_t q = 0; q < preps.size(); q++)
-            if (preps[q].x == o.x_dev && preps[q].m == o.m && preps[q].k == o.w->k) pi = (int)q;
+            if (preps[q].x == o.x_dev && preps[q].m == o.m && preps[q].k == o.w->k &&
+                preps[q].norm_w == o.norm_w_dev && (!o.norm_w_dev || preps[q].eps == o.norm_eps))
+                pi = (int)q;
         if (pi < 0) {
-            prep_key pk{o.x_dev, o.m, o.w->k, 0, 0, 0};
+            prep_key pk{o.x_dev, o.m, o.w->k, o.norm_w_dev, o.norm_eps, 0, 0, 0};
             const size_t kp = (size_t)o.w->kc * XQ4G_KCHUNK;
             pk.img_off = img_bytes;
             img_bytes += align((size_t)o.m * kp * 2);
@@ -518,7 +544,8 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     for (size_t q = 0; q < preps.size(); q++) {
         const prep_key &pk = preps[q];
         ptab[q] = xq4_chain_prep_dev{pk.x, (uint16_t *)(img + pk.img_off), (float *)(img + pk.tbl_off),
-                                     (unsigned *)(img + pk.max_off), pk.m, pk.k, (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK, 0};
+                                     (unsigned *)(img + pk.max_off), pk.m, pk.k, (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK,
+                                     pk.norm_w != nullptr, (const uint16_t *)pk.norm_w, pk.eps, 0};
     }
     for (int i = 0; i < n_ops; i++) {
         const int pi = op_prep[(size_t)i];

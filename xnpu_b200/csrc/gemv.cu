@@ -647,16 +647,56 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     const uint16_t *x = reinterpret_cast<const uint16_t *>(p.x);
     const int kp = p.kc * XQ4G_KCHUNK, runs = p.k / 8, total_runs = p.m * runs;
     __shared__ unsigned smax[8];
+    __shared__ float sinv[8];
     if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
     for (int i = threadIdx.x; i < p.kc * 32; i += kPrepThreads) p.tbl[i] = 0.f;
+    if (p.norm) {
+        // RMSNorm (crates/xnpu-cli/src/main.rs:4714-4724): warp w sums the
+        // squares of token w, lane-strided then a fixed butterfly, so the
+        // result is the same on every run; inv = 1 / sqrt(mean + eps)
+        const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        if (w < p.m) {
+            float ss = 0.f;
+            for (int i = lane; i < p.k; i += 32) {
+                const float v = __uint_as_float((uint32_t)x[(size_t)w * p.k + i] << 16);
+                ss = __fadd_rn(ss, __fmul_rn(v, v));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+            if (lane == 0) sinv[w] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.k), p.eps)));
+        }
+    }
     __syncthreads();
-    for (int r = threadIdx.x; r < total_runs; r += kPrepThreads) {
+    // one run of 8 activations (of token `tok`, starting at element kk), as
+    // the GEMV consumes them: normalised first when the op asks for it
+    const auto run_words = [&](int r, int tok, int kk, uint32_t (&w)[4]) {
         const uint4 v = xq4d::ldcg_v4(x + 8 * (size_t)r);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+        if (p.norm) {
+            const float inv = sinv[tok];
+            const uint4 g = *reinterpret_cast<const uint4 *>(p.norm_w + kk);
+            const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const float lo = __fmul_rn(__fmul_rn(__uint_as_float(w[h] << 16), inv), __uint_as_float(gw[h] << 16));
+                const float hi = __fmul_rn(__fmul_rn(__uint_as_float(w[h] & 0xFFFF0000u), inv),
+                                           __uint_as_float(gw[h] & 0xFFFF0000u));
+                w[h] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+                       ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+            }
+        }
+    };
+    for (int r = threadIdx.x; r < total_runs; r += kPrepThreads) {
+        const int tok = r / runs;
+        uint32_t w[4];
+        run_words(r, tok, 8 * (r - tok * runs), w);
         unsigned mx = 0;
 #pragma unroll
         for (int h = 0; h < 4; h++) mx = max(mx, max(w[h] & 0x7FFFu, (w[h] >> 16) & 0x7FFFu));
-        if (mx) atomicMax(&smax[r / runs], mx);
+        if (mx) atomicMax(&smax[tok], mx);
     }
     __syncthreads();
     const int lane = threadIdx.x & 31;
@@ -669,8 +709,8 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
             kk = 8 * (r - tok * runs);
             float f1, f2;
             pow2_split(tok_exponent(smax[tok]), f1, f2);
-            const uint4 v = xq4d::ldcg_v4(x + 8 * (size_t)r);
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            uint32_t w[4];
+            run_words(r, tok, kk, w);
             uint32_t h2[4];
 #pragma unroll
             for (int h = 0; h < 4; h++) {
@@ -784,18 +824,43 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                     break;
                 }
                 const float *rd = red + (size_t)buf * kConsumerWarps * 128;  // [warp][tok][row]
-                for (int oo = lane; oo < op.m * 16; oo += 32) {
+                for (int base = 0; base < op.m * 16; base += 32) {  // uniform trip count: SwiGLU pairs lanes
+                    const int oo = base + lane;
                     const int tok = oo >> 4, r = oo & 15;
-                    float sum = 0.f;
-#pragma unroll
-                    for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
                     const int row = rb * XQ4G_ROWS + r;
-                    if (row < op.n) {
+                    const bool valid = oo < op.m * 16 && row < op.n;
+                    float sum = 0.f;
+                    if (valid) {
+#pragma unroll
+                        for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
                         if (op.xh) {  // undo 2^-24 and the token's power of two (exact)
                             float f1, f2;
                             pow2_split(24 - tok_exponent(op.xh_max[tok]), f1, f2);
                             sum = sum * f1 * f2;
                         }
+                    }
+                    if (op.swiglu) {
+                        // rows 2i (gate) and 2i+1 (up) sit in neighbouring
+                        // lanes; the reference's swiglu_bf16 (main.rs:
+                        // 4732-4745) on the op's bf16 outputs
+                        const float hb = __bfloat162float(__float2bfloat16_rn(sum));
+                        const float u = __shfl_xor_sync(0xffffffffu, hb, 1);
+                        if (valid && !(r & 1)) {
+                            const float gs = __fmul_rn(hb, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-hb))));
+                            reinterpret_cast<__nv_bfloat16 *>(op.y)[(size_t)tok * (op.n >> 1) + (row >> 1)] =
+                                __float2bfloat16_rn(__fmul_rn(gs, u));
+                        }
+                        continue;
+                    }
+                    if (!valid) continue;
+                    if (op.residual) {  // add_bf16 (main.rs:4726-4730) of the op's bf16 output
+                        const size_t ri = (size_t)tok * op.n + row;
+                        const float hb = __bfloat162float(__float2bfloat16_rn(sum));
+                        const float res = __uint_as_float((uint32_t)xq4d::ldcg_u16(op.residual + ri) << 16);
+                        reinterpret_cast<__nv_bfloat16 *>(op.y)[ri] = __float2bfloat16_rn(__fadd_rn(hb, res));
+                        continue;
+                    }
+                    {
                         const size_t idx = (size_t)tok * ystride + yoff + row;
                         uint32_t bits;
                         if (op.out_f32) {

@@ -55,6 +55,12 @@ __device__ __forceinline__ uint4 ldcg_v4(const void *p)
                  : "memory");
     return r;
 }
+__device__ __forceinline__ uint16_t ldcg_u16(const uint16_t *p)
+{
+    uint16_t v;
+    asm volatile("ld.global.cg.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned ld_acquire_gpu_u32(const unsigned *p)
 {
     unsigned v;

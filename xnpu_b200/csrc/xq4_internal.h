@@ -74,6 +74,11 @@ struct xq4_chain_op_dev {
     int shard;
     int n_total, row_off;
     long long inbox_off;  // the op's first word in an inbox half
+    // Epilogues (not with shard): y = RNE(RNE(Wx) + residual), or SwiGLU of
+    // the row pairs (2i, 2i+1) into y[tok][n/2].
+    const uint16_t *residual;
+    int swiglu;
+    int pad3;
 };
 
 // The chain's communicator side (nranks == 1: no sharded op).
@@ -97,7 +102,10 @@ struct xq4_chain_prep_dev {
     uint16_t *img;
     float *tbl;
     unsigned *max;
-    int m, k, kc, pad;
+    int m, k, kc, norm;   // norm: RMS-normalise x with norm_w first
+    const uint16_t *norm_w;
+    float eps;
+    int pad;
 };
 
 struct xq4_weight {

@@ -225,15 +225,21 @@ class Chain:
     reference's chained op packets, built once and submitted together).
 
     ``ops`` is a list of (weight, x_ptr, y_ptr, m, out_dtype, wait_prev[,
-    comm]) with raw device pointers (ints) and an optional communicator
-    handle for a column-sharded op; see xq4_chain_create."""
+    comm][, glue]) with raw device pointers (ints), an optional
+    communicator handle for a column-sharded op and an optional dict of
+    fused decode-step glue: {"norm_w": ptr, "eps": float, "residual": ptr,
+    "swiglu": bool}; see xq4_chain_create."""
 
     def __init__(self, dev, ops):
         arr = (_lib.ChainOp * len(ops))()
         for i, op in enumerate(ops):
+            op = list(op)
+            glue = op.pop() if isinstance(op[-1], dict) else {}
             w, xp, yp, m, od, wp = op[:6]
             comm = op[6] if len(op) > 6 else None
-            arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0, getattr(comm, "value", comm))
+            arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0, getattr(comm, "value", comm),
+                                  glue.get("norm_w"), float(glue.get("eps", 1e-5)), glue.get("residual"),
+                                  1 if glue.get("swiglu") else 0)
         h = ctypes.c_void_p()
         check(lib().xq4_chain_create(dev.handle, arr, len(ops), ctypes.byref(h)))
         self._h, self.dev, self.n_ops = h, dev, len(ops)

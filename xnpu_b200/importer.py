@@ -192,7 +192,19 @@ def golden_x(k):
 
 
 # ------------------------------------------------------------------ the import
-def import_layers(model, out, layers=None, shapes=LLAMA_SHAPES, cols=8, prefix="model.layers", log=print):
+def interleave_rows(a, b):
+    """Rows a0, b0, a1, b1, ...: a gate/up projection whose SwiGLU a GEMV
+    epilogue can apply within one 16-row block (both halves of a pair in
+    neighbouring rows)."""
+    if a.shape != b.shape:
+        raise ValueError("gate and up differ in shape")
+    out = np.empty((2 * a.shape[0], a.shape[1]), dtype=a.dtype)
+    out[0::2], out[1::2] = a, b
+    return out
+
+
+def import_layers(model, out, layers=None, shapes=LLAMA_SHAPES, cols=8, prefix="model.layers", log=print,
+                  interleave_gateup=False):
     st = SafeTensors(model)
     out = Path(out)
     out.mkdir(parents=True, exist_ok=True)
@@ -200,7 +212,8 @@ def import_layers(model, out, layers=None, shapes=LLAMA_SHAPES, cols=8, prefix="
         idx = {int(nm.split(".")[2]) for nm in st.names() if nm.startswith(prefix + ".")}
         layers = sorted(idx)
     meta = {"group_size": GROUP, "cols": cols, "layers": list(layers), "shapes": {},
-            "quantizer": "symmetric amax/7 per 32-wide group, bf16 scale (RNE), q = rint(w/s) in [-8, 7]"}
+            "quantizer": "symmetric amax/7 per 32-wide group, bf16 scale (RNE), q = rint(w/s) in [-8, 7]",
+            "gateup_rows": "interleaved (gate_i, up_i)" if interleave_gateup else "gate then up"}
     total = 0
     for li, n_layer in enumerate(layers):
         for shape, (parts, tsi) in shapes.items():
@@ -208,7 +221,10 @@ def import_layers(model, out, layers=None, shapes=LLAMA_SHAPES, cols=8, prefix="
             k = mats[0].shape[1]
             if any(m.ndim != 2 or m.shape[1] != k for m in mats):
                 raise ValueError(f"layer {n_layer} {shape}: parts disagree on K")
-            w = np.concatenate(mats, axis=0)
+            if interleave_gateup and shape == "gateup":
+                w = interleave_rows(*mats)
+            else:
+                w = np.concatenate(mats, axis=0)
             n = w.shape[0]
             q, s = quantize_group32(w)
             packed = pack_l1(q, s, tsi, cols)
@@ -231,8 +247,10 @@ def main(argv=None):
     ap.add_argument("--out", required=True)
     ap.add_argument("--layers", type=int, nargs="*", default=None, help="layer indices (default: all)")
     ap.add_argument("--cols", type=int, default=8)
+    ap.add_argument("--interleave-gateup", action="store_true",
+                    help="write gateup rows as gate_i, up_i pairs (for a chain op's fused SwiGLU)")
     args = ap.parse_args(argv)
-    import_layers(args.model, args.out, args.layers, cols=args.cols)
+    import_layers(args.model, args.out, args.layers, cols=args.cols, interleave_gateup=args.interleave_gateup)
     return 0
 
 
