@@ -12,20 +12,18 @@ Gate and up are one fused "gateup" projection, as in the reference's own
 layer chain (crates/xnpu-cli/src/main.rs:2464, :2488: 4 GEMV shapes per
 layer, qkv / o / gateup / down); the weight bytes are those of the two.
 
-The step is ONE launch of the GEMV chain kernel over the 128 projections
-(xq4_chain_run, after a small kernel that prepares the fp16 activation
-images; the ops are independent because each reads its fixed activation).
-The same chain with every op waiting for the previous one (a real decode
-step's dependency order) and the 128 separate GEMV launches (one CUDA graph)
-are timed beside it (``other_step_forms_ms``).
+On one GPU the step is ONE launch of the GEMV chain kernel over the 128
+projections (xq4_chain_run, after a small kernel that prepares the fp16
+activation images; the ops are independent because each reads its fixed
+activation).  The same chain with every op waiting for the previous
+one (a real decode step's dependency order) and the 128 separate GEMV
+launches (one CUDA graph) are timed beside it (``other_step_forms_ms``).
 
-On N GPUs (torchrun, one process per GPU) every projection is
-column-sharded N ways: each rank's chain computes its rows and stores them
-into the peers' inboxes over NVLink peer memory while it runs, and copies
-the peers' rows in at the end, so every rank ends the step with every
-output (the separate-launch form gathers per projection inside each GEMV,
-xq4_linear_sharded_fused).  The step is the same token, so scaling is
-"strong".  The line also reports the lm_head 4096->128256 (f32 logits)
+On N GPUs (torchrun, one process per GPU) the FFN gateup projection is
+column-sharded N ways, with the all-gather inside the GEMV kernel over NVLink
+peer memory (xq4_linear_sharded_fused); QKV, O and down are replicated; the
+step is the 128 launches in one CUDA graph.  The step is the same token, so
+scaling is "strong".  The line also reports the lm_head 4096->128256 (f32 logits)
 sharded the same way.
 
 Metric: tokens/s (higher is better); GB/s of algorithmic bytes (packed codes
@@ -49,7 +47,7 @@ sys.path.insert(0, str(ROOT))
 
 LAYERS = 32
 SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gateup", 28672, 4096), ("down", 4096, 14336)]
-SHARDED = ("qkv", "o", "gateup", "down")  # column-sharded over ranks at N > 1
+SHARDED = ("gateup",)  # column-sharded over ranks; the rest are replicas
 # DRAM bytes (read + write) per launch of each projection at one GPU, from
 #   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #       --clock-control none -k regex:gemv --csv python bench.py --layers 4 --steps 1
@@ -326,31 +324,33 @@ def main():
             graph.replay()
     barrier()
 
-    # The step as ONE chain launch (xq4_chain_run).  Every projection reads
-    # its fixed activation (the reference's projection-stream benchmark,
-    # main.rs:2487-2499), so the ops are independent (wait_prev = 0); the
-    # same chain with every op waiting for the previous one (the dependency
-    # order of a real decode step) is timed beside it.  At N > 1 every
-    # projection is column-sharded over the ranks: each rank computes its
-    # rows and sends them to the peers while the chain runs, and every rank
-    # ends the launch with all outputs.
+    # One GPU: the step as ONE chain launch (xq4_chain_run).  Every
+    # projection reads its fixed activation (the reference's projection-stream
+    # benchmark, main.rs:2487-2499), so the ops are independent (wait_prev =
+    # 0); the same chain with every op waiting for the previous one (the
+    # dependency order of a real decode step) is timed beside it.
     chains = {}
-    for wp in (0, 1):
-        chains[wp] = hal.Chain(dev, [(layer[name], xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, wp,
-                                      comm if (comm is not None and name in SHARDED) else None)
-                                     for layer in weights for name, n, k in SHAPES])
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                chains[wp].run(stream)
-    barrier()
+    if world == 1:
+        for wp in (0, 1):
+            chains[wp] = hal.Chain(dev, [(layer[name], xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, wp)
+                                         for layer in weights for name, n, k in SHAPES])
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    chains[wp].run(stream)
+        barrier()
 
     # device-timed steps (inputs resident in HBM)
     with ClockSampler(local) as clk:
-        ms = timed(lambda: chains[0].run(stream), args.steps)
+        if world == 1:
+            ms = timed(lambda: chains[0].run(stream), args.steps)
+            per_step = 2  # the activation prep kernel + the chain kernel
+        else:
+            ms = timed(graph.replay, args.steps)
     clocks = clk.summary()
-    launches = 2 * args.steps  # per step: the activation prep kernel + the chain kernel
-    alt = {"separate_launches_graph_ms": timed(graph.replay, args.steps),
-           "chain_dependent_ms": timed(lambda: chains[1].run(stream), args.steps)}
+    launches = per_step * args.steps
+    alt = {"separate_launches_graph_ms": timed(graph.replay, args.steps)}
+    if world == 1:
+        alt["chain_dependent_ms"] = timed(lambda: chains[1].run(stream), args.steps)
     for c in chains.values():
         c.destroy()
 
@@ -401,20 +401,22 @@ def main():
             "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
                                    "gateup 4096x28672, down 14336x4096), M=1",
                        "group": 32, "layers": LAYERS, "batch": 1,
-                       "parallelism": ("single GPU" if world == 1 else
-                                       f"every projection column-sharded x{world}; each rank's rows reach the "
-                                       "peers over NVLink peer memory during the chain launch; every rank ends "
-                                       "the step with all outputs"),
+                       "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world}, rows gathered by the GEMV over NVLink peer memory; qkv/o/down replicated",
                        "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
             "gbs": step_bytes * (1e3 / ms) / 1e9,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "gemv_chain_kernel (the step's 128 GEMVs in one launch, m=1)",
-                         "traffic": (CHAIN_DRAM_PER_STEP * LAYERS / 32 if (CHAIN_DRAM_PER_STEP and world == 1)
-                                     else None),
-                         "traffic_unit": "bytes per launch (ncu, 4-layer chain scaled by bytes to 32 layers)",
-                         "algorithmic_bytes_per_launch": gpu_step_bytes,
-                         "region": "one chain launch per step (per GPU)"},
+            "roofline": ({"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "peak_kind": peak_kind,
+                          "kernel": "gemv_chain_kernel (the step's 128 GEMVs in one launch, m=1)",
+                          "traffic": (CHAIN_DRAM_PER_STEP * LAYERS / 32 if CHAIN_DRAM_PER_STEP else None),
+                          "traffic_unit": "bytes per launch (ncu, 4-layer chain scaled by bytes to 32 layers)",
+                          "algorithmic_bytes_per_launch": gpu_step_bytes,
+                          "region": "one chain launch per step"}
+                         if world == 1 else
+                         {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                          "frac": achieved / peak, "peak_kind": peak_kind,
+                          "kernel": "gemv_kernel<1> (decode GEMV, m=1)", "traffic": None,
+                          "algorithmic_bytes_per_launch": gpu_step_bytes / LAYERS / len(SHAPES),
+                          "region": "all GEMV launches of the timed steps (CUDA graph replays)"}),
             "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()},
             "other_step_forms_ms": alt,
             "e2e": e2e,
@@ -440,9 +442,9 @@ def main():
 
 def e2e_run(dev, weights, comm, world, args):
     """Same step through the public C ABI with host buffers: one pinned H2D of
-    the step's activations, one xq4_chain_submit of the step's 128 GEMVs on
-    the device queue, xq4_wait, one D2H of every output -- timed on the host
-    clock."""
+    the step's activations, 128 xq4_linear submits on the device queue, one
+    D2H of every output, xq4_wait -- timed on the host clock."""
+    import ctypes
     import torch
     from xnpu_b200 import hal, lib, synth
     from xnpu_b200._lib import check
@@ -462,15 +464,31 @@ def e2e_run(dev, weights, comm, world, args):
     hx = torch.empty(x_bytes, dtype=torch.uint8).pin_memory()
     hy = torch.empty(y_bytes, dtype=torch.uint8).pin_memory()
     hx.numpy()[:] = synth.synth_x(1, x_bytes // 2, 5).reshape(-1).view(np.uint8)
+    seq = ctypes.c_uint64()
 
-    # the step is one chain submit (ops independent, as the timed step)
-    chain = hal.Chain(dev, [(layer[name], xb.device_ptr() + k_off[k], yb.device_ptr() + y_off[(li, name)],
-                             1, 0, 0, comm if (comm is not None and name in SHARDED) else None)
-                            for li, layer in enumerate(weights) for name, n, k in SHAPES])
+    chain = None
+    if comm is None:  # one GPU: the step is one chain submit (ops independent, as the timed step)
+        chain = hal.Chain(dev, [(layer[name], xb.device_ptr() + k_off[k], yb.device_ptr() + y_off[(li, name)],
+                                 1, 0, 0) for li, layer in enumerate(weights) for name, n, k in SHAPES])
 
     def one():
         check(L.xq4_buffer_upload(xb.handle, hx.data_ptr(), 0, x_bytes))
-        check(L.xq4_wait(dev.handle, chain.submit(), 60_000_000_000))
+        if chain is not None:
+            chain.submit()
+            check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
+            check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
+            return
+        for li, layer in enumerate(weights):
+            for name, n, k in SHAPES:
+                if comm is not None and name in SHARDED:
+                    xp = xb.device_ptr() + k_off[k]
+                    yp = yb.device_ptr() + y_off[(li, name)]
+                    check(L.xq4_linear_sharded_fused(comm, layer[name].handle, xp, yp, 1, 0,
+                                                     dev.stream_handle()))
+                else:
+                    check(L.xq4_linear(dev.handle, layer[name].handle, xb.handle, k_off[k], yb.handle,
+                                       y_off[(li, name)], 1, 0, ctypes.byref(seq)))
+        check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
         check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
 
     import torch.distributed as dist
@@ -486,12 +504,14 @@ def e2e_run(dev, weights, comm, world, args):
         t = torch.tensor([dt], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    chain.destroy()
+    if chain is not None:
+        chain.destroy()
     xb.destroy()
     yb.destroy()
-    path = ("xq4_buffer_upload -> xq4_chain_submit (the step's 128 GEMVs" +
-            (", column-sharded with the rows exchanged over NVLink" if comm is not None else "") +
-            ") -> xq4_wait -> xq4_buffer_download (pinned host buffers)")
+    path = ("xq4_buffer_upload -> xq4_chain_submit (the step's 128 GEMVs) -> xq4_wait -> xq4_buffer_download "
+            "(pinned host buffers)" if chain is not None else
+            "xq4_buffer_upload -> 128 x xq4_linear (gateup: xq4_linear_sharded_fused) -> xq4_wait -> "
+            "xq4_buffer_download (pinned host buffers)")
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
             "ms_per_step": dt * 1e3, "path": path}
 

@@ -197,7 +197,10 @@ typedef struct xq4_chain_op {
     int out_dtype;
     int wait_prev;
     /* NULL, or the communicator over which the op is column-sharded as
-     * xq4_linear_sharded_fused: w is this rank's row shard (every rank's of
+     * xq4_linear_sharded_fused.  Not enabled in this build: a communicator
+     * of more than one rank makes xq4_chain_create return XQ4_ENOTSUP (the
+     * path is not yet verified on GPUs).  The intended behaviour:
+     * w is this rank's row shard (every rank's of
      * the same size), y_dev the full m x n_total output.  A rank's rows
      * reach the peers' inboxes while the chain runs; each rank copies the
      * peers' rows into y_dev before the next op that waits, or at the end

@@ -94,43 +94,6 @@ def _rank_main(rank, world, id_q, res_q):
                 bits = ctypes.c_uint32()
                 check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
                 out[("fault", m, f32)] = bits.value
-        # a chain with column-sharded ops (rows sent while the chain runs,
-        # copied in before the op that waits and at the end): A = sharded
-        # (external x, fp16 path), B = replicated, C = sharded reading A's
-        # gathered output (waits for it, bf16 path); twice in a row
-        x = synth.synth_x(1, k, 58)
-        xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
-        q2 = synth.unpack_codes_signed(synth.synth_codes(2048, k, 59))
-        s2 = synth.synth_scales(2048, k, 59)
-        w2 = hal.Weight.import_(dev, synth.planes_bytes(synth.pack_codes_signed(q2), s2),
-                                hal.layout_desc(hal.XQ4_LAYOUT_PLANES, 2048, k))
-        ya = torch.full((1, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-        yb = torch.full((1, 2048), float("nan"), dtype=torch.bfloat16, device="cuda")
-        yc = torch.full((1, n), float("nan"), dtype=torch.bfloat16, device="cuda")
-        chain = hal.Chain(dev, [(w, xd.data_ptr(), ya.data_ptr(), 1, 0, 0, comm),
-                                (w2, xd.data_ptr(), yb.data_ptr(), 1, 0, 0),
-                                (w, ya.data_ptr(), yc.data_ptr(), 1, 0, 1, comm)])
-        for rep in range(2):
-            for yy in (ya, yb, yc):
-                yy.fill_(float("nan"))
-            chain.run()
-            torch.cuda.synchronize()
-            out[("chain_bits", rep)] = (ya.cpu().view(torch.int16).numpy().tobytes(),
-                                        yc.cpu().view(torch.int16).numpy().tobytes())
-            # C's own rows: the single-op GEMV (bf16 path) on the gathered A
-            yl = torch.empty((1, ns), dtype=torch.bfloat16, device="cuda")
-            check(L.xq4_linear_raw(w.handle, ya.data_ptr(), yl.data_ptr(), 1, 0, st))
-            torch.cuda.synchronize()
-            own = yc[:, rank * ns:(rank + 1) * ns]
-            out[("chain_own", rep)] = bool(torch.equal(yl.view(torch.int16), own.view(torch.int16)))
-        got = synth.bf16_bits_to_f32(ya.cpu().view(torch.int16).numpy().view(np.uint16))[:, rows]
-        ref = synth.bf16_bits_to_f32(O.round_bf16(O.gemv_q(q[rows], s[rows], x)))
-        out[("chain_parity",)] = rel_metrics(got, ref)[:2]
-        bits = ctypes.c_uint32()
-        check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
-        out[("fault", "chain")] = bits.value
-        chain.destroy()
-        w2.destroy()
         # a peer that never makes the call: this rank's kernel gives up after
         # its bounded wait (about 2 s), reports fault bit 0x8 and the context
         # stays usable
@@ -177,17 +140,8 @@ def test_linear_sharded_two_gpus():
     assert all(p.exitcode == 0 for p in procs), (results, [p.exitcode for p in procs])
     for rank, status, out in results:
         assert status == "ok", (rank, out)
-    # the sharded chain: every rank holds the same full outputs
-    by_rank = {rank: out for rank, _, out in results}
-    for rep in range(2):
-        assert by_rank[0][("chain_bits", rep)] == by_rank[1][("chain_bits", rep)], rep
-    for rank, status, out in results:
         for key, val in out.items():
-            if key[0] == "chain_bits":
-                continue
-            if key[0] == "chain_parity":
-                assert val[0] <= 1e-2 and val[1] <= 1e-3, (rank, key, val)
-            elif key[0] in ("fused", "lone_after", "chain_own"):
+            if key[0] in ("fused", "lone_after"):
                 assert val, (rank, key, "fused gather differs from the NCCL path")
             elif key[0] == "fault":
                 assert val == 0, (rank, key, val)

@@ -410,7 +410,13 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     }
     xq4_chain_p2p p2p{};
     p2p.nranks = 1;
-    if (comm) {  // maps the inboxes at the first use (collective)
+    // Column-sharded chain ops are built (the kernel's inbox path) but not
+    // enabled: their first two-GPU test run did not finish, for a reason not
+    // yet found, so a communicator with more than one rank is refused.
+    if (comm && xq4_comm_nranks(comm) > 1)
+        return xq4_fail(XQ4_ENOTSUP, "column-sharded chain ops are not enabled in this build "
+                                     "(use xq4_linear_sharded_fused per projection)");
+    if (comm) {
         if (int rc = xq4_comm_chain_p2p(comm, dev, &p2p)) return rc;
     }
     long long inbox_words = 0;
