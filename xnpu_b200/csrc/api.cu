@@ -449,7 +449,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.shard = o.comm && p2p.nranks > 1;
         d.residual = (const uint16_t *)o.residual_dev;
         d.swiglu = o.swiglu != 0;
-        d.pad3 = 0;
+        d.wait_parity = 0;
         if (o.residual_dev || o.swiglu || o.norm_w_dev) {
             if (o.comm) return xq4_fail(XQ4_EINVAL, "op %d: fused glue with a sharded op", i);
             if ((o.residual_dev || o.swiglu) && o.out_dtype != XQ4_OUT_BF16)
@@ -471,6 +471,9 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
                                 inbox_words);
         }
     }
+    // the consumers' op barrier completes once per waiting op (op 0 never waits)
+    for (int i = 1, waits = 0; i < n_ops; i++)
+        if (tab[(size_t)i].wait_prev) tab[(size_t)i].wait_parity = waits++ & 1;
     // segments: a new one starts at op 0 and at every op that waits
     for (int i = 0; i < n_ops;) {
         int j = i + 1;

@@ -609,7 +609,8 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 #endif
 constexpr int kChainStages = XQ4_CHAIN_STAGES;
 static_assert(kStageChunks == XQ4_GEMV_STAGE_CHUNKS_ABI, "the host splits chain work in these stages");
-constexpr int kChainBarBytes = ((2 * kChainStages + 2 * kRedBufs) * 8 + 127) & ~127;
+// ring full/empty, reduce full/free, and the consumers' op barrier
+constexpr int kChainBarBytes = ((2 * kChainStages + 2 * kRedBufs + 1) * 8 + 127) & ~127;
 constexpr size_t kChainRingOff = kChainBarBytes + (size_t)kRedBufs * kConsumerWarps * 128 * 4;
 constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kStageBytes;
 static_assert(kChainRingOff % 128 == 0, "ring alignment");
@@ -749,6 +750,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
     uint64_t *empty = full + kChainStages;
     uint64_t *red_full = empty + kChainStages;
     uint64_t *red_free = red_full + kRedBufs;
+    uint64_t *op_bar = red_free + kRedBufs;  // consumers meet here before an op that waits
     float *red = reinterpret_cast<float *>(smem + kChainBarBytes);
     uint8_t *ring = smem + kChainRingOff;
 
@@ -764,6 +766,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
             xq4d::mbar_init(&red_full[b], kConsumerWarps);
             xq4d::mbar_init(&red_free[b], 1);
         }
+        xq4d::mbar_init(op_bar, kConsumerWarps);
         xq4d::fence_barrier_init();
     }
     __syncthreads();
@@ -949,6 +952,10 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
     for (int o = 0; o < n_ops; o++) {
         const xq4_chain_op_dev op = ops[o];
         if (op.wait_prev && o > 0) {
+            // warp 0 sees every CTA's count (acquire), then the consumer
+            // warps meet on an mbarrier (release / acquire within the CTA):
+            // a bounded wait, so a warp that gave up earlier cannot hold the
+            // others forever
             if (warp == 0 && lane == 0) {
                 const uint64_t t0 = xq4d::global_ns();
                 while (xq4d::ld_acquire_gpu_u32(&done[o - 1]) < (unsigned)G) {
@@ -958,7 +965,9 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                     }
                 }
             }
-            xq4d::named_bar_sync(1, kConsumerThreads);
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(op_bar);
+            if (!xq4d::mbar_wait(op_bar, (uint32_t)op.wait_parity)) atomicOr(&g_xq4_fault, XQ4_FAULT_CHAIN_WAIT);
         }
         const int tok = g < op.m ? g : 0;
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK

@@ -78,7 +78,7 @@ struct xq4_chain_op_dev {
     // the row pairs (2i, 2i+1) into y[tok][n/2].
     const uint16_t *residual;
     int swiglu;
-    int pad3;
+    int wait_parity;      // phase parity of the consumers' op barrier at this op (waiting ops before it, mod 2)
 };
 
 // The chain's communicator side (nranks == 1: no sharded op).
