@@ -12,6 +12,7 @@ context usable.  Skipped with fewer than two GPUs.
 """
 import os
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -131,12 +132,21 @@ def test_linear_sharded_two_gpus():
     procs = [ctx.Process(target=_rank_main, args=(r, 2, id_q, res_q)) for r in range(2)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    results = [res_q.get(timeout=5) for _ in range(2)]
+    # Read the results before joining: a child cannot exit while its queued
+    # result is still in the pipe, and a child killed in the middle of a put
+    # leaves a message the reader would wait on forever.  The results stay
+    # small (flags and metrics, no output arrays).
+    results, deadline = [], time.monotonic() + 300
+    try:
+        for _ in range(2):
+            results.append(res_q.get(timeout=max(1.0, deadline - time.monotonic())))
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
     assert all(p.exitcode == 0 for p in procs), (results, [p.exitcode for p in procs])
     for rank, status, out in results:
         assert status == "ok", (rank, out)
