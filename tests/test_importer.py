@@ -146,3 +146,14 @@ def test_imported_l1_on_gpu(dev, tmp_path):
         assert_parity(y.reshape(1, n), want, f"imported {shape}")
         w.destroy()
         torch.cuda.synchronize()
+
+
+def test_importer_command_line(tmp_path):
+    model = tmp_path / "tiny.safetensors"
+    _tiny_model(model, layers=2)
+    out = tmp_path / "w4"
+    assert I.main(["--model", str(model), "--out", str(out), "--layers", "1", "--interleave-gateup"]) == 0
+    meta = json.loads((out / "meta.json").read_text())
+    assert meta["layers"] == [1] and meta["gateup_rows"].startswith("interleaved")
+    assert sorted(p.name for p in out.iterdir()) == sorted(
+        ["meta.json"] + [f"layer01_{s}.bin" for s in I.LLAMA_SHAPES] + [f"golden_{s}.bin" for s in I.LLAMA_SHAPES])

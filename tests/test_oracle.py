@@ -207,3 +207,40 @@ def test_chunk_partial_sum_rule():
     out = synth.bf16_bits_to_f32(O.sum_chunk_partials(parts))
     # 1 + 2^-8 + 1 = 2.00390625 in f32; 2^-8 is below half a bf16 ulp at 2
     assert out.tolist() == [2.0, 0.0]
+
+
+def _bf(v):
+    """f32 values -> bf16 bits (RNE), independent of the oracle."""
+    b = np.asarray(v, dtype=np.float32).view(np.uint32)
+    return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _f(b):
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def test_glue_restatements():
+    """rms_norm_bf16 / add_bf16 / swiglu_bf16 (crates/xnpu-cli/src/main.rs:
+    4714-4745) against a direct numpy transcription with the reference's
+    operation order: a sequential f32 sum of squares, (x * inv) * w, one
+    RNE per output."""
+    rng = np.random.default_rng(7)
+    k = 512
+    x = _bf(rng.normal(0, 2, size=(3, k)))
+    w = _bf(rng.normal(1, 0.1, size=k))
+    got = O.rms_norm(x, w, eps=1e-5)
+    for t in range(3):
+        s = np.float32(0)
+        for v in _f(x[t]):
+            s = np.float32(s + np.float32(v * v))
+        inv = np.float32(1) / np.sqrt(np.float32(s / np.float32(k) + np.float32(1e-5)))
+        want = _bf((_f(x[t]) * inv).astype(np.float32) * _f(w))
+        assert np.array_equal(got[t], want), t
+    a, b = _bf(rng.normal(size=1000)), _bf(rng.normal(size=1000))
+    assert np.array_equal(O.add_bf16(a, b), _bf(_f(a) + _f(b)))
+    gu = _bf(rng.normal(0, 3, size=(2, 64)))
+    g, u = _f(gu[:, :32]), _f(gu[:, 32:])
+    sig = (np.float32(1) / (np.float32(1) + np.exp(-g).astype(np.float32))).astype(np.float32)
+    want = _bf((g * sig).astype(np.float32) * u)
+    d = np.abs(O.swiglu(gu).astype(np.int32) - want.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() < 0.05  # numpy's exp and libm's may differ in the last f32 bit
