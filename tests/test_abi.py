@@ -54,3 +54,28 @@ def test_device_open_without_gpu_fails_cleanly():
     with pytest.raises(_lib.Xq4Error) as ei:
         hal.Device.open_default()
     assert ei.value.status == _lib.XQ4_ENODEV
+
+
+@pytest.mark.parametrize("cname,pystruct", [("xq4_layout_desc", _lib.LayoutDesc),
+                                            ("xq4_device_info", _lib.DeviceInfo),
+                                            ("xq4_chain_op", _lib.ChainOp)])
+def test_struct_layouts_match_the_header(tmp_path, cname, pystruct):
+    """Every field of the ctypes mirror sits at the C compiler's offset, and
+    the sizes agree (a C program built against include/xq4.h prints them)."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in pystruct._fields_]
+    src = tmp_path / "layout.c"
+    body = "".join(f'    printf("{f} %zu\\n", offsetof({cname}, {f}));\n' for f in fields)
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "xq4.h"\nint main(void) {{\n{body}'
+                   f'    printf("sizeof %zu\\n", sizeof({cname}));\n    return 0;\n}}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-std=c11", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for f in fields:
+        assert int(out[f]) == getattr(pystruct, f).offset, (cname, f)
+    assert int(out["sizeof"]) == ctypes.sizeof(pystruct), cname
