@@ -230,35 +230,17 @@ extern "C" int xq4_weight_import(xq4_device *dev, const void *src, size_t src_le
         cudaGetLastError();
         return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for weight: %s", bytes, cudaGetErrorString(e));
     }
-    // decode-GEMV workspace: split-row-block partials, then zeroed counters
-    const int ws_ctas = xq4_gemv_ws_ctas();
-    const size_t ws_bytes = xq4_gemv_ws_bytes(n, ws_ctas);
-    const size_t part_bytes = ws_bytes - (size_t)xq4g_nb(n) * sizeof(unsigned);
-    void *ws = nullptr;
-    e = cudaMalloc(&ws, ws_bytes);
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        cudaFree(p);
-        return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the GEMV workspace: %s", ws_bytes, cudaGetErrorString(e));
-    }
     e = cudaMemcpyAsync(p, host.data(), bytes, cudaMemcpyHostToDevice, dev->stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync((char *)ws + part_bytes, 0, ws_bytes - part_bytes, dev->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(dev->stream);
     if (e != cudaSuccess) {
         cudaFree(p);
-        cudaFree(ws);
         return cuda_fail(e, "weight upload");
     }
     xq4_weight *w = new (std::nothrow) xq4_weight();
     if (!w) {
         cudaFree(p);
-        cudaFree(ws);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
     }
-    w->d_ws = ws;
-    w->ws.part = (float *)ws;
-    w->ws.cnt = (unsigned *)((char *)ws + part_bytes);
-    w->ws.ctas = ws_ctas;
     w->dev = dev;
     w->ordinal = dev->ordinal;
     w->n = n;
@@ -278,8 +260,6 @@ extern "C" int xq4_weight_destroy(xq4_weight *w)
     cudaSetDevice(w->ordinal);
     cudaDeviceSynchronize();  // no queued op may still use it
     cudaError_t e = cudaFree(w->d_pack);
-    const cudaError_t e2 = cudaFree(w->d_ws);
-    if (e == cudaSuccess) e = e2;
     delete w;
     if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
     return XQ4_OK;
@@ -345,7 +325,7 @@ static int launch_linear(const xq4_weight *w, const void *x, void *y, int m, int
         return xq4_fail(XQ4_EINVAL, "x and y must be 16-byte aligned");
     const int f32 = out_dtype == XQ4_OUT_F32;
     const bool gemv = xq4_use_gemv(m);
-    cudaError_t e = gemv ? xq4_launch_gemv(w->d_pack, w->n, w->k, x, m, y, f32, w->ws, st)
+    cudaError_t e = gemv ? xq4_launch_gemv(w->d_pack, w->n, w->k, x, m, y, f32, st)
                          : xq4_launch_gemm(w->d_pack, w->n, w->k, x, m, y, f32, st);
     if (e != cudaSuccess) return cuda_fail(e, gemv ? "gemv launch" : "gemm launch");
     return XQ4_OK;

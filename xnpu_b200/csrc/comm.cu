@@ -180,7 +180,7 @@ extern "C" int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w, const voi
     const size_t slice = (size_t)m * ns;  // elements per rank
     char *gather = (char *)(m == 1 ? y_full_dev : ws_dev);
     void *mine = gather + (size_t)comm->rank * slice * esz;
-    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
+    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st)
                         : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
     ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
@@ -270,7 +270,7 @@ extern "C" int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w, c
     const size_t slice = (size_t)m * ns;  // elements per rank
     char *gather = (char *)(m == 1 ? y_full_dev : ws);
     void *mine = gather + (size_t)comm->rank * slice * esz;
-    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, w->ws, st)
+    e = xq4_use_gemv(m) ? xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st)
                         : xq4_launch_gemm(w->d_pack, w->n, w->k, x_dev, m, mine, f32, st);
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "shard linear launch: %s", cudaGetErrorString(e));
     ncclResult_t r = a->AllGather(mine, gather, slice, dt, comm->nccl, st);
@@ -423,10 +423,10 @@ extern "C" int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w, con
         p.half_words = XQ4_FUSED_MAX_VALUES;
         p.cnt = (unsigned *)comm->inbox.local;
         p.epoch = (unsigned *)(comm->inbox.local + 4);
-        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32, w->ws,
+        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32,
                             (cudaStream_t)stream, &p);
     } else {  // one rank: the shard is the whole matrix
-        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32, w->ws,
+        e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32,
                             (cudaStream_t)stream);
     }
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "fused sharded launch: %s", cudaGetErrorString(e));

@@ -1074,9 +1074,8 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
 
 // m in 1..16 per launch; larger m is split into 16-token slices.
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y, int out_f32,
-                            const xq4_gemv_ws &ws, cudaStream_t st, const xq4_p2p_out *p2p)
+                            cudaStream_t st, const xq4_p2p_out *p2p)
 {
-    (void)ws;
     const xq4_p2p_out none{};
     if (p2p && m > 16) return cudaErrorInvalidValue;  // one launch per sharded call
     static_assert(xh_offset(2) + 128 + (size_t)kStages * kStageBytes <= (size_t)kMaxSmem, "bf16 plan too large");
@@ -1143,13 +1142,6 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, done, p2p);
 }
-
-size_t xq4_gemv_ws_bytes(int n, int ctas)
-{
-    return (size_t)ctas * 2 * 2 * 128 * sizeof(float) + (size_t)xq4g_nb(n) * sizeof(unsigned);
-}
-
-int xq4_gemv_ws_ctas() { return sm_count_of_current_device() * kCtasPerSm; }
 
 // Read and clear this unit's fault word on the current device.
 unsigned int xq4_take_fault_gemv()

@@ -20,14 +20,6 @@ int xq4_repack_rows(const void *src, size_t src_len, const xq4_layout_desc *desc
 #ifdef __CUDACC__
 #include <cuda_runtime.h>
 
-// A weight resident in HBM, in XQ4G layout.
-// Decode-GEMV workspace of one weight: split-row-block partials and one
-// arrival counter per row block (zero between launches).
-struct xq4_gemv_ws {
-    float *part;
-    unsigned *cnt;
-    int ctas;          // largest grid the partial area holds
-};
 
 // Column-sharded GEMV with the gather inside the kernel.  Every output value
 // travels to each peer as one 64-bit word in the peer's inbox: the value's
@@ -108,6 +100,7 @@ struct xq4_chain_prep_dev {
     int pad;
 };
 
+// A weight resident in HBM, in XQ4G layout.
 struct xq4_weight {
     struct xq4_device *dev;
     int ordinal;       // device ordinal (destroy does not touch `dev`)
@@ -115,8 +108,6 @@ struct xq4_weight {
     int nb, kc;        // row blocks, 64-K chunks
     uint8_t *d_pack;   // xq4g_bytes(n, k) bytes
     size_t bytes;
-    void *d_ws;        // GEMV workspace allocation (xq4_gemv_ws_bytes)
-    struct xq4_gemv_ws ws;
 };
 
 // Smallest m that runs the tensor-core GEMM; below it the decode GEMV (in
@@ -131,12 +122,8 @@ static inline bool xq4_use_gemv(int m) { return m < XQ4_GEMM_MIN_M; }
 // Kernel launchers (gemv.cu, gemm_tc.cu, dequant.cu).  All return cudaError_t
 // of the launch; arguments are validated by the callers in api.cu.
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
-                            int out_f32, const struct xq4_gemv_ws &ws, cudaStream_t st,
+                            int out_f32, cudaStream_t st,
                             const struct xq4_p2p_out *p2p = nullptr);
-// Workspace bytes for an n-row weight and a grid of `ctas` (partials first,
-// then nb counters), and the grid the current device runs the GEMV with.
-size_t xq4_gemv_ws_bytes(int n, int ctas);
-int xq4_gemv_ws_ctas();
 // One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
 // n_ops + 1 zeroed counters (left zeroed at the end of the launch).
 cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, unsigned *done,
