@@ -662,3 +662,88 @@ void q4o_swiglu_bf16(const uint16_t *x, int half, uint16_t *out)
         out[i] = q4o_f32_to_bf16(g * (1.f / (1.f + expf(-g))) * u);
     }
 }
+
+/* Llama rotate-half RoPE tables at one position: inv_freq = base^(-j/64),
+ * c[j] = cos(pos * inv), s[j] = sin(pos * inv), j < 64.
+ * crates/xnpu-cli/src/main.rs:4817-4827 */
+void q4o_rope_table(int pos, float base, float *c, float *s)
+{
+    for (int j = 0; j < 64; j++) {
+        const float inv = powf(base, -(float)j / 64.f);
+        const float a = (float)pos * inv;
+        c[j] = cosf(a);
+        s[j] = sinf(a);
+    }
+}
+
+/* RoPE on `heads` heads of 128: out[j] = RNE(x1 c - x2 s), out[64+j] =
+ * RNE(x2 c + x1 s).  crates/xnpu-cli/src/main.rs:4829-4839 */
+void q4o_rope_apply(const uint16_t *x, const float *c, const float *s, int heads, uint16_t *out)
+{
+    for (int h = 0; h < heads; h++) {
+        const int o = h * 128;
+        for (int j = 0; j < 64; j++) {
+            const float x1 = q4o_bf16_to_f32(x[o + j]);
+            const float x2 = q4o_bf16_to_f32(x[o + 64 + j]);
+            out[o + j] = q4o_f32_to_bf16(x1 * c[j] - x2 * s[j]);
+            out[o + 64 + j] = q4o_f32_to_bf16(x2 * c[j] + x1 * s[j]);
+        }
+    }
+}
+
+/* Per-head RMSNorm over 128 (the q/k norm applied after RoPE), weights [128]
+ * shared by every head.  crates/xnpu-cli/src/main.rs:4844-4857 */
+void q4o_qk_rms_bf16(const uint16_t *x, int len, const uint16_t *w, uint16_t *out)
+{
+    for (int h = 0; h < len / 128; h++) {
+        const int o = h * 128;
+        float sum = 0.f;
+        for (int j = 0; j < 128; j++) {
+            const float v = q4o_bf16_to_f32(x[o + j]);
+            sum += v * v;
+        }
+        const float inv = 1.f / sqrtf(sum / 128.f + 1e-5f);
+        for (int j = 0; j < 128; j++)
+            out[o + j] = q4o_f32_to_bf16(q4o_bf16_to_f32(x[o + j]) * inv * q4o_bf16_to_f32(w[j]));
+    }
+}
+
+/* GQA decode attention for the token at position pos over a bf16 KV cache
+ * laid out [nkv][cache_seq][128]: per q-head, scores = (K q) / sqrt(128)
+ * summed sequentially over the 128 dims, softmax with the max subtracted,
+ * acc = sum_t w_t v_t in ascending t, out = RNE(acc / sum).  The scalar path
+ * of crates/xnpu-cli/src/main.rs:4967-5033. */
+int q4o_attention_bf16(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, int pos, int cache_seq,
+                       int heads, int nkv, uint16_t *out)
+{
+    if (heads <= 0 || nkv <= 0 || heads % nkv || pos < 0 || pos >= cache_seq) return Q4O_EINVAL;
+    const int s = pos + 1, group = heads / nkv;
+    float *sc = (float *)malloc(sizeof(float) * (size_t)s);
+    if (!sc) return Q4O_EINVAL;
+    for (int kv = 0; kv < nkv; kv++) {
+        const size_t base = (size_t)kv * cache_seq * 128;
+        for (int h = kv * group; h < (kv + 1) * group; h++) {
+            const int qo = h * 128;
+            float mx = -INFINITY;
+            for (int t = 0; t < s; t++) {
+                float d = 0.f;
+                for (int j = 0; j < 128; j++)
+                    d += q4o_bf16_to_f32(kc[base + (size_t)t * 128 + j]) * q4o_bf16_to_f32(q[qo + j]);
+                sc[t] = d / sqrtf(128.f);
+                mx = fmaxf(mx, sc[t]);
+            }
+            float sum = 0.f;
+            for (int t = 0; t < s; t++) {
+                sc[t] = expf(sc[t] - mx);
+                sum += sc[t];
+            }
+            float acc[128];
+            for (int j = 0; j < 128; j++) acc[j] = 0.f;
+            for (int t = 0; t < s; t++)
+                for (int j = 0; j < 128; j++) acc[j] += sc[t] * q4o_bf16_to_f32(vc[base + (size_t)t * 128 + j]);
+            for (int j = 0; j < 128; j++) out[qo + j] = q4o_f32_to_bf16(acc[j] / sum);
+        }
+    }
+    free(sc);
+    return Q4O_OK;
+}

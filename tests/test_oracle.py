@@ -244,3 +244,53 @@ def test_glue_restatements():
     want = _bf((g * sig).astype(np.float32) * u)
     d = np.abs(O.swiglu(gu).astype(np.int32) - want.astype(np.int32))
     assert d.max() <= 1 and (d > 0).mean() < 0.05  # numpy's exp and libm's may differ in the last f32 bit
+
+
+def test_rope_and_qk_norm_restatements():
+    """rope_table / rope_apply / qk_rms_bf16 (main.rs:4817-4857)."""
+    c, s = O.rope_table(0)
+    assert np.all(c == 1) and np.all(s == 0)
+    rng = np.random.default_rng(11)
+    x = _bf(rng.normal(0, 2, size=4 * 128))
+    assert np.array_equal(O.rope_apply(x, c, s), x)  # position 0: identity
+    pos, base = 37, 10000.0
+    c, s = O.rope_table(pos, base)
+    j = np.arange(64, dtype=np.float64)
+    a = pos * base ** (-j / 64)
+    assert np.allclose(c, np.cos(a), rtol=0, atol=2e-6) and np.allclose(s, np.sin(a), rtol=0, atol=2e-6)
+    got = O.rope_apply(x, c, s).reshape(4, 128)
+    xf = _f(x).reshape(4, 128)
+    x1, x2 = xf[:, :64], xf[:, 64:]
+    want = np.concatenate([_bf((x1 * c).astype(np.float32) - (x2 * s).astype(np.float32)),
+                           _bf((x2 * c).astype(np.float32) + (x1 * s).astype(np.float32))], axis=1)
+    assert np.array_equal(got, want)
+    w = _bf(rng.normal(1, 0.1, size=128))
+    got = O.qk_rms(x, w).reshape(4, 128)
+    for h in range(4):
+        acc = np.float32(0)
+        for v in xf[h]:
+            acc = np.float32(acc + np.float32(v * v))
+        inv = np.float32(1) / np.sqrt(np.float32(acc / np.float32(128) + np.float32(1e-5)))
+        assert np.array_equal(got[h], _bf((xf[h] * inv).astype(np.float32) * _f(w))), h
+
+
+def test_attention_restatement():
+    """attention_bf16 (main.rs:4967-5033): one position returns its V row;
+    a longer context agrees with a float64 softmax to the bf16 grain."""
+    rng = np.random.default_rng(12)
+    heads, nkv, seq = 8, 2, 40
+    q = _bf(rng.normal(size=heads * 128))
+    kc = _bf(rng.normal(size=(nkv, seq, 128)))
+    vc = _bf(rng.normal(size=(nkv, seq, 128)))
+    out0 = O.attention(q, kc, vc, 0, seq, heads, nkv).reshape(heads, 128)
+    for h in range(heads):
+        assert np.array_equal(out0[h], vc[h // (heads // nkv), 0]), h
+    pos = 29
+    out = _f(O.attention(q, kc, vc, pos, seq, heads, nkv)).reshape(heads, 128).astype(np.float64)
+    qf, kf, vf = _f(q).reshape(heads, 128), _f(kc), _f(vc)
+    for h in range(heads):
+        kv = h // (heads // nkv)
+        sc = kf[kv, :pos + 1].astype(np.float64) @ qf[h].astype(np.float64) / np.sqrt(128.0)
+        p = np.exp(sc - sc.max())
+        ref = (p / p.sum()) @ vf[kv, :pos + 1].astype(np.float64)
+        assert np.all(np.abs(out[h] - ref) <= 2.0 ** -7 * np.abs(ref) + 1e-6), h
