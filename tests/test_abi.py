@@ -79,3 +79,23 @@ def test_struct_layouts_match_the_header(tmp_path, cname, pystruct):
     for f in fields:
         assert int(out[f]) == getattr(pystruct, f).offset, (cname, f)
     assert int(out["sizeof"]) == ctypes.sizeof(pystruct), cname
+
+
+def test_null_arguments_are_rejected_without_a_device():
+    """The entry points validate their arguments before touching CUDA: NULL
+    handles give XQ4_EINVAL and a message, NULL destroys are no-ops."""
+    L = _lib.lib()
+    out = ctypes.c_void_p()
+    seq = ctypes.c_uint64()
+    op = _lib.ChainOp()
+    for rc in (L.xq4_chain_create(None, ctypes.byref(op), 1, ctypes.byref(out)),
+               L.xq4_chain_run(None, None),
+               L.xq4_chain_submit(None, None, ctypes.byref(seq)),
+               L.xq4_linear_raw(None, None, None, 1, 0, None),
+               L.xq4_linear_sharded_fused(None, None, None, None, 1, 0, None),
+               L.xq4_linear_sharded_noalloc(None, None, None, None, 1, 0, None)):
+        assert rc == _lib.XQ4_EINVAL
+        assert L.xq4_last_error_string()
+    assert L.xq4_chain_destroy(None) == _lib.XQ4_OK
+    assert L.xq4_weight_destroy(None) == _lib.XQ4_OK
+    assert L.xq4_comm_destroy(None) == _lib.XQ4_OK
