@@ -187,7 +187,13 @@ int xq4_linear_raw(const xq4_weight *w, const void *x_dev, void *y_dev,
  * aligned to its element.  The op table is copied to the device at create;
  * the pointers must stay valid while the chain is used.  A chain runs on one
  * stream at a time (its completion counters are per chain).  A dependency
- * wait that runs out (2 s) sets fault bit 0x10. */
+ * wait that runs out (2 s) sets fault bit 0x10.  The kernel's CTAs (2 per SM)
+ * wait for one another, so all of them must be resident at once: create
+ * returns XQ4_ENOTSUP when the device cannot hold them (the environment
+ * variable XQ4_RESIDENT_CTAS_PER_SM, for diagnostics, replaces the occupancy
+ * figure this check uses).  With a sharded op, run and submit return
+ * XQ4_ETIMEDOUT once the communicator is unusable (see
+ * xq4_linear_sharded_fused). */
 typedef struct xq4_chain xq4_chain;
 typedef struct xq4_chain_op {
     const xq4_weight *w;
@@ -197,18 +203,18 @@ typedef struct xq4_chain_op {
     int out_dtype;
     int wait_prev;
     /* NULL, or the communicator over which the op is column-sharded as
-     * xq4_linear_sharded_fused.  Not enabled in this build: a communicator
-     * of more than one rank makes xq4_chain_create return XQ4_ENOTSUP (the
-     * path is not yet verified on GPUs).  The intended behaviour:
-     * w is this rank's row shard (every rank's of
-     * the same size), y_dev the full m x n_total output.  A rank's rows
-     * reach the peers' inboxes while the chain runs; each rank copies the
-     * peers' rows into y_dev before the next op that waits, or at the end
-     * of the launch.  All sharded ops of a chain use one communicator, their
-     * m x n_total summed is at most XQ4_FUSED_MAX_VALUES, and every rank
-     * creates and runs its chain (the same op shapes) together with the
-     * others: create is collective when it maps the inboxes, as the first
-     * xq4_linear_sharded_fused call. */
+     * xq4_linear_sharded_fused: w is this rank's row shard (every rank's of
+     * the same size), y_dev the full m x n_total output (m x n_total/2 with
+     * swiglu: each rank computes the SwiGLU of its own row pairs and the
+     * intermediate is what is gathered).  A rank's rows reach the peers'
+     * inboxes while the chain runs; each rank copies the peers' rows into
+     * y_dev before the next op that waits, or at the end of the launch.  All
+     * sharded ops of a chain use one communicator, their m x n_total
+     * (n_total/2 with swiglu) summed is at most XQ4_FUSED_MAX_VALUES, and
+     * every rank creates and runs its chain (the same op shapes, on GPUs
+     * with the same SM count) together with the others: create is
+     * collective when it maps the inboxes, as the first
+     * xq4_linear_sharded_fused call.  A sharded op takes no residual. */
     struct xq4_comm *comm;
     /* Decode-step glue fused into the op (NULL / 0 = none; not with comm),
      * each as the reference computes it (crates/xnpu-cli/src/main.rs:
@@ -301,10 +307,17 @@ int xq4_linear_sharded(xq4_comm *comm, const xq4_weight *w_shard,
  * order.  The first call on a communicator allocates and maps the inboxes
  * (2 x XQ4_FUSED_MAX_VALUES x 8 bytes per rank, collective, device-wide
  * synchronising): make it before any stream capture.  A peer value that
- * does not arrive within 2 s sets fault bit 0x8 (xq4_device_fault).  Do not
- * run the call beside other kernels that wait on peers: each CTA waits for
- * the matching CTA of every peer.  Stands in for the column split with a host
- * gather of the per-column C sections (w4u_read_c,
+ * does not arrive within 2 s sets fault bit 0x8 (xq4_device_fault), and
+ * leaves the communicator unusable: the ranks' call counts are then out of
+ * step, so the kernel that gave up marks the communicator on every rank.
+ * From then on this rank's calls (and runs of chains with sharded ops on the
+ * communicator) return XQ4_ETIMEDOUT; a peer's next call exchanges nothing
+ * (its y_full holds its own rows only), sets fault bit 0x8 and marks it the
+ * same way.  Destroy and re-create the communicator to go on.  Each CTA
+ * waits for the matching CTA of every peer, so the whole grid must be
+ * resident: XQ4_ENOTSUP when the device cannot hold it.  Do not run the call
+ * beside other kernels that wait on peers.  Stands in for the column split
+ * with a host gather of the per-column C sections (w4u_read_c,
  * crates/xnpu-cli/src/main.rs:3066-3091). */
 #define XQ4_FUSED_MAX_VALUES (4u * 1024u * 1024u)
 int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w_shard, const void *x_dev,
@@ -317,14 +330,20 @@ int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w_shard, const vo
  * afford cudaMalloc/cudaFree (cudaFree synchronises the device), or a
  * foreign-language caller with no device allocator.  For m > 1 the gather
  * stages through a fixed scratch array of XQ4_NOALLOC_SCRATCH_BYTES inside
- * the library (held by every GPU that loads it until the process exits);
- * m * n_total * element size beyond that is rejected with XQ4_EINVAL.  The
- * first call on a device looks up the array's device address (set-up): make
- * that first call before any stream capture.  All calls share the array, so
- * calls that overlap on the GPU race on it.  NCCL sets up a communicator's
- * connections, and allocates its own buffers, at the communicator's first
- * collective: run one collective on it (for instance one xq4_linear_sharded
- * call) before relying on this entry point to allocate nothing. */
+ * the library; m * n_total * element size beyond that is rejected with
+ * XQ4_EINVAL.  The array is committed on a device when the library's module
+ * holding it is loaded there (CUDA loads modules lazily: at the first sharded
+ * call on the device, or at this entry point's first call, whose set-up looks
+ * up the array's device address), and stays until the process exits.  So
+ * the entry point allocates nothing only after that set-up: a caller that
+ * reserves the GPU's memory up front should make one call (m > 1) first, and
+ * make it before any stream capture.  All calls share the array, so calls
+ * that overlap on the GPU (other streams, other threads) race on it:
+ * serialise them, for instance on one stream.  NCCL sets up a
+ * communicator's connections, and allocates its own buffers, at the
+ * communicator's first collective: run one collective on it (for instance
+ * one xq4_linear_sharded call) before relying on this entry point to
+ * allocate nothing. */
 #define XQ4_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int xq4_linear_sharded_noalloc(xq4_comm *comm, const xq4_weight *w_shard,
                                const void *x_dev, void *y_full_dev,

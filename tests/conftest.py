@@ -28,3 +28,18 @@ def dev():
     d = hal.Device.open_default()
     yield d
     d.close()
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """Print every parity figure the GPU tests recorded (tests/parity.py):
+    the floored max relative error the asserts use, the unfloored one and
+    the count of outputs above 1e-2 unfloored."""
+    try:
+        import parity
+    except ImportError:
+        return
+    lines = parity.summary_lines()
+    if lines:
+        terminalreporter.section("parity")
+        for line in lines:
+            terminalreporter.write_line(line)

@@ -186,3 +186,36 @@ def test_chain_rejects_bad_ops(dev):
             hal.Chain(dev, [op])
     h = ctypes.c_void_p()
     assert lib().xq4_chain_create(dev.handle, None, 0, ctypes.byref(h)) != 0
+
+
+def test_chain_refused_when_its_grid_cannot_be_resident():
+    """The chain's CTAs wait for one another, so chain create refuses a device
+    that cannot hold its whole grid at once: emulated with the diagnostic
+    override of the occupancy figure (one CTA per SM), in a child process."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    code = (
+        "import sys, torch, numpy as np\n"
+        f"sys.path.insert(0, {str(root)!r})\n"
+        "from xnpu_b200 import hal, synth, _lib\n"
+        "dev = hal.Device.open(0)\n"
+        "src = synth.planes_bytes(synth.synth_codes(256, 4096, 5), synth.synth_scales(256, 4096, 5))\n"
+        "w = hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, 256, 4096))\n"
+        "x = torch.zeros((1, 4096), dtype=torch.bfloat16, device='cuda')\n"
+        "y = torch.zeros((1, 256), dtype=torch.bfloat16, device='cuda')\n"
+        "try:\n"
+        "    hal.Chain(dev, [(w, x.data_ptr(), y.data_ptr(), 1, 0, 0)])\n"
+        "    print('created')\n"
+        "except _lib.Xq4Error as e:\n"
+        "    print('status', e.status)\n"
+    )
+    env = dict(os.environ, XQ4_RESIDENT_CTAS_PER_SM="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert f"status {6}" in r.stdout, r.stdout  # XQ4_ENOTSUP
+    env["XQ4_RESIDENT_CTAS_PER_SM"] = ""  # the real occupancy: two CTAs per SM fit
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert "created" in r.stdout, (r.stdout, r.stderr[-2000:])

@@ -3,12 +3,24 @@
 Two processes (one per GPU) import their row shard of one matrix, run the
 shard's GEMV (m < 25) or GEMM (m >= 25), all-gather the slices with NCCL
 (xq4_linear_sharded) and must both hold the full output, within the parity
-bars of the single-GPU tests against the oracle over the full matrix.  For
+bars of the single-GPU tests against the oracle over the full matrix.  The
+same call without a workspace (xq4_linear_sharded_noalloc, its gather staged
+in the library's fixed scratch array) must give the identical bits.  For
 m < 16 the same call with the gather fused into the GEMV over peer memory
 (xq4_linear_sharded_fused) must give the identical bits on both ranks, twice
-in a row, with no fault bit raised; a fused call that only one rank makes
-must end after the kernel's bounded wait with fault bit 0x8, leaving the
-context usable.  Skipped with fewer than two GPUs.
+in a row, with no fault bit raised.
+
+A chain with column-sharded ops (a gate/up projection with its SwiGLU
+epilogue, whose 1-per-pair intermediate is gathered; an f32 projection; a
+replicated op; and an op that waits for the gathered intermediate and reads
+it) must give, on both ranks and in two runs, the bits of the same chain run
+unsharded on the full weights.
+
+A fused call that only one rank makes must end after the kernel's bounded
+wait with fault bit 0x8, leaving the context usable; the communicator is
+then unusable on both ranks: the rank that gave up refuses its next call,
+and the peer's next call exchanges nothing, raises fault bit 0x8 and is then
+refused too.  Skipped with fewer than two GPUs.
 """
 import os
 import socket
@@ -39,7 +51,7 @@ def _rank_main(rank, world, id_q, res_q):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
     from oracle import oracle as O
-    from xnpu_b200 import hal, lib, synth
+    from xnpu_b200 import _lib, hal, lib, synth
     from xnpu_b200._lib import check
     from test_gpu_kernels import rel_metrics
 
@@ -82,6 +94,12 @@ def _rank_main(rank, world, id_q, res_q):
                 ref = synth.bf16_bits_to_f32(O.round_bf16(ref))
             max_rel, mae, _ = rel_metrics(got, ref)
             out[(m, f32)] = (max_rel, mae)
+            # no workspace: the gather stages through the library's scratch array
+            yn = torch.full((m, n), float("nan"), dtype=yd.dtype, device="cuda")
+            check(L.xq4_linear_sharded_noalloc(comm, w.handle, xd.data_ptr(), yn.data_ptr(), m, f32, st))
+            torch.cuda.synchronize()
+            iv = torch.int32 if f32 else torch.int16
+            out[("noalloc", m, f32)] = bool(torch.equal(yn.view(iv), yd.view(iv)))
             if m < 16:
                 # the same call with the gather fused into the GEMV over peer
                 # memory: identical bits on every rank, twice in a row (the
@@ -95,6 +113,7 @@ def _rank_main(rank, world, id_q, res_q):
                 bits = ctypes.c_uint32()
                 check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
                 out[("fault", m, f32)] = bits.value
+        out.update(_sharded_chain(dev, comm, rank, world, L))
         # a peer that never makes the call: this rank's kernel gives up after
         # its bounded wait (about 2 s), reports fault bit 0x8 and the context
         # stays usable
@@ -114,6 +133,21 @@ def _rank_main(rank, world, id_q, res_q):
             id_q.put("lone done")
         else:
             assert id_q.get(timeout=120) == "lone done"
+        # the communicator is unusable from now on, on both ranks
+        x = synth.synth_x(1, k, 58)
+        xd = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+        yf = torch.full((1, n), float("nan"), dtype=torch.bfloat16, device="cuda")
+        rc = L.xq4_linear_sharded_fused(comm, w.handle, xd.data_ptr(), yf.data_ptr(), 1, 0, st)
+        torch.cuda.synchronize()
+        bits = ctypes.c_uint32()
+        check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
+        rc2 = L.xq4_linear_sharded_fused(comm, w.handle, xd.data_ptr(), yf.data_ptr(), 1, 0, st)
+        torch.cuda.synchronize()
+        if rank == 0:  # it gave up itself: refused on the host
+            out[("poisoned",)] = rc == _lib.XQ4_ETIMEDOUT and rc2 == _lib.XQ4_ETIMEDOUT
+        else:  # its peer poisoned it: the kernel exchanges nothing and flags it, then refused
+            out[("poisoned",)] = rc == 0 and bits.value == 0x8 and rc2 == _lib.XQ4_ETIMEDOUT
+        out[("poisoned_detail",)] = (rc, bits.value, rc2)
         w.destroy()
         res_q.put((rank, "ok", out))
     except Exception as e:
@@ -122,6 +156,62 @@ def _rank_main(rank, world, id_q, res_q):
     finally:
         L.xq4_comm_destroy(comm)
         dev.close()
+
+
+def _sharded_chain(dev, comm, rank, world, L):
+    """A chain with column-sharded ops against the same chain unsharded."""
+    import ctypes
+    from xnpu_b200 import hal, synth
+    from xnpu_b200._lib import check
+
+    def imp(n, k, seed, r0=0, r1=0):
+        src = synth.planes_bytes(synth.synth_codes(n, k, seed), synth.synth_scales(n, k, seed))
+        return hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=r0, row_end=r1))
+
+    k, ng, nl, nr, nd = 4096, 8192, 8192, 1024, 1024  # gate/up (interleaved) rows, f32 op rows, replicated, down
+    shard = lambda n: (rank * n // world, (rank + 1) * n // world)  # noqa: E731
+    wg_s, wg_f = imp(ng, k, 71, *shard(ng)), imp(ng, k, 71)
+    wl_s, wl_f = imp(nl, k, 72, *shard(nl)), imp(nl, k, 72)
+    wr = imp(nr, k, 73)
+    wd = imp(nd, ng // 2, 74)  # reads the gathered SwiGLU intermediate
+    x = torch.from_numpy(synth.synth_x(1, k, 75).view(np.int16)).cuda().view(torch.bfloat16)
+
+    def outputs():
+        return (torch.full((1, ng // 2), float("nan"), dtype=torch.bfloat16, device="cuda"),
+                torch.full((1, nl), float("nan"), dtype=torch.float32, device="cuda"),
+                torch.full((1, nr), float("nan"), dtype=torch.bfloat16, device="cuda"),
+                torch.full((1, nd), float("nan"), dtype=torch.bfloat16, device="cuda"))
+
+    def ops(ys, sharded):
+        c = comm if sharded else None
+        return [(wg_s if sharded else wg_f, x.data_ptr(), ys[0].data_ptr(), 1, 0, 0, c, {"swiglu": True}),
+                (wl_s if sharded else wl_f, x.data_ptr(), ys[1].data_ptr(), 1, 1, 0, c),
+                (wr, x.data_ptr(), ys[2].data_ptr(), 1, 0, 0),
+                (wd, ys[0].data_ptr(), ys[3].data_ptr(), 1, 0, 1)]
+
+    ref = outputs()
+    full = hal.Chain(dev, ops(ref, False))
+    full.run()
+    torch.cuda.synchronize()
+    got = outputs()
+    sh = hal.Chain(dev, ops(got, True))
+    res = {}
+    for rep in range(2):  # both inbox halves
+        for t in got:
+            t.fill_(float("nan"))
+        sh.run()
+        torch.cuda.synchronize()
+        for i, (a, b) in enumerate(zip(got, ref)):
+            iv = torch.int32 if a.dtype == torch.float32 else torch.int16
+            res[("chain", i, rep)] = bool(torch.equal(a.view(iv), b.view(iv)))
+    bits = ctypes.c_uint32()
+    check(L.xq4_device_fault(dev.handle, ctypes.byref(bits)))
+    res[("fault", "chain")] = bits.value
+    sh.destroy()
+    full.destroy()
+    for w in (wg_s, wg_f, wl_s, wl_f, wr, wd):
+        w.destroy()
+    return res
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
@@ -151,8 +241,10 @@ def test_linear_sharded_two_gpus():
     for rank, status, out in results:
         assert status == "ok", (rank, out)
         for key, val in out.items():
-            if key[0] in ("fused", "lone_after"):
-                assert val, (rank, key, "fused gather differs from the NCCL path")
+            if key[0] in ("fused", "lone_after", "noalloc", "chain", "poisoned"):
+                assert val, (rank, key, "differs from the reference path", out.get(("poisoned_detail",)))
+            elif key[0] == "poisoned_detail":
+                continue
             elif key[0] == "fault":
                 assert val == 0, (rank, key, val)
             elif key[0] == "lone_fault":

@@ -373,6 +373,7 @@ struct xq4_chain {
     unsigned *d_done;         // prep table, fp16 images
     xq4_chain_prep_dev *d_preps;
     xq4_chain_p2p p2p;        // sharded ops' communicator (nranks 1: none)
+    xq4_comm *comm;           // that communicator, or NULL
 };
 
 extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out)
@@ -390,14 +391,17 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     }
     xq4_chain_p2p p2p{};
     p2p.nranks = 1;
-    // Column-sharded chain ops are built (the kernel's inbox path) but not
-    // enabled: their first two-GPU test run did not finish, for a reason not
-    // yet found, so a communicator with more than one rank is refused.
-    if (comm && xq4_comm_nranks(comm) > 1)
-        return xq4_fail(XQ4_ENOTSUP, "column-sharded chain ops are not enabled in this build "
-                                     "(use xq4_linear_sharded_fused per projection)");
+    CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
+    {
+        const cudaError_t e = xq4_gemv_chain_prepare();
+        if (e == cudaErrorCooperativeLaunchTooLarge)
+            return xq4_fail(XQ4_ENOTSUP, "chain: its ops wait for one another across CTAs, so all of its CTAs (2 per "
+                                         "SM) must be resident at once, and this device cannot hold them");
+        if (e != cudaSuccess) return cuda_fail(e, "chain kernel set-up");
+    }
     if (comm) {
         if (int rc = xq4_comm_chain_p2p(comm, dev, &p2p)) return rc;
+        if (int rc = xq4_comm_check_usable(comm)) return rc;
     }
     long long inbox_words = 0;
     for (int i = 0; i < n_ops; i++) {
@@ -431,7 +435,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.swiglu = o.swiglu != 0;
         d.wait_parity = 0;
         if (o.residual_dev || o.swiglu || o.norm_w_dev) {
-            if (o.comm) return xq4_fail(XQ4_EINVAL, "op %d: fused glue with a sharded op", i);
+            if (o.comm && o.residual_dev) return xq4_fail(XQ4_EINVAL, "op %d: a residual epilogue on a sharded op", i);
             if ((o.residual_dev || o.swiglu) && o.out_dtype != XQ4_OUT_BF16)
                 return xq4_fail(XQ4_EINVAL, "op %d: a residual or SwiGLU epilogue writes bf16 only", i);
             if (o.residual_dev && o.swiglu) return xq4_fail(XQ4_EINVAL, "op %d: residual and SwiGLU together", i);
@@ -445,7 +449,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.inbox_off = 0;
         if (d.shard) {
             d.inbox_off = inbox_words;
-            inbox_words += (long long)o.m * d.n_total;
+            inbox_words += (long long)o.m * (d.swiglu ? d.n_total / 2 : d.n_total);
             if (inbox_words > (long long)XQ4_FUSED_MAX_VALUES)
                 return xq4_fail(XQ4_EINVAL, "sharded ops: m x n_total summed to %lld, above XQ4_FUSED_MAX_VALUES",
                                 inbox_words);
@@ -477,7 +481,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     };
     // bytes of op j's output
     const auto y_bytes = [&](int j) {
-        const size_t rows = tab[(size_t)j].swiglu ? (size_t)tab[(size_t)j].n / 2 : (size_t)tab[(size_t)j].n_total;
+        const size_t rows = (size_t)tab[(size_t)j].n_total / (tab[(size_t)j].swiglu ? 2 : 1);
         return (size_t)ops[j].m * rows * (ops[j].out_dtype == XQ4_OUT_F32 ? 4 : 2);
     };
     std::vector<prep_key> preps;
@@ -557,7 +561,8 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     }
     xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
                                                 (unsigned *)(base + tab_bytes),
-                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes), p2p};
+                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes), p2p,
+                                                p2p.nranks > 1 ? comm : nullptr};
     if (!c) {
         cudaFree(mem);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -582,6 +587,8 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
 {
     xq4_clear_error();
     if (!chain) return xq4_fail(XQ4_EINVAL, "NULL chain");
+    if (chain->comm)
+        if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
     CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
                              (cudaStream_t)stream),
@@ -594,6 +601,8 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
     xq4_clear_error();
     if (!dev || !chain) return xq4_fail(XQ4_EINVAL, "NULL argument");
     if (chain->dev != dev) return xq4_fail(XQ4_EINVAL, "chain of another device");
+    if (chain->comm)
+        if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
                              dev->stream),

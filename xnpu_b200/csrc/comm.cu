@@ -81,12 +81,16 @@ struct xq4_comm {
     ncclComm_t nccl;
     int rank, nranks;
     // fused gather (created by the first xq4_linear_sharded_fused call): CTA
-    // count at 0, epoch at 4, the two inbox halves from kInboxHead
+    // count at 0, epoch at 4, poison word at 8, the two inbox halves from
+    // kInboxHead
     shared_buf inbox{};
     void *xchg = nullptr;               // device scratch for exchanging IPC handles
+    unsigned *poison_host = nullptr;    // host-mapped flag: a kernel gave up waiting for a peer
+    unsigned *poison_dev = nullptr;     // its device address
 };
 
 static constexpr size_t kInboxHead = 256;
+static constexpr size_t kPoisonOff = 8;
 static constexpr size_t kInboxHalfBytes = (size_t)XQ4_FUSED_MAX_VALUES * sizeof(unsigned long long);
 
 extern "C" int xq4_comm_unique_id(void *id_out)
@@ -149,6 +153,7 @@ extern "C" int xq4_comm_destroy(xq4_comm *comm)
         cudaFree(comm->inbox.local);
     }
     if (comm->xchg) cudaFree(comm->xchg);
+    if (comm->poison_host) cudaFreeHost(comm->poison_host);
     ncclResult_t r = a->CommDestroy(comm->nccl);
     delete comm;
     if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
@@ -350,6 +355,23 @@ namespace {
 // into it before that.
 int setup_inbox(xq4_comm *comm)
 {
+    if (!comm->poison_host) {
+        void *h = nullptr;
+        cudaError_t e = cudaHostAlloc(&h, 64, cudaHostAllocMapped);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return xq4_fail(XQ4_ENOMEM, "cudaHostAlloc for the communicator's poison flag: %s", cudaGetErrorString(e));
+        }
+        memset(h, 0, 64);
+        void *d = nullptr;
+        e = cudaHostGetDevicePointer(&d, h, 0);
+        if (e != cudaSuccess) {
+            cudaFreeHost(h);
+            return xq4_fail(XQ4_ECUDA, "cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
+        }
+        comm->poison_host = (unsigned *)h;
+        comm->poison_dev = (unsigned *)d;
+    }
     cudaError_t e = cudaMalloc(&comm->xchg, 64 * 2 * (XQ4_MAX_RANKS + 1));
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -372,6 +394,24 @@ int setup_inbox(xq4_comm *comm)
 int xq4_comm_nranks(const xq4_comm *comm) { return comm->nranks; }
 int xq4_comm_rank(const xq4_comm *comm) { return comm->rank; }
 
+int xq4_comm_check_usable(const xq4_comm *comm)
+{
+    if (comm->poison_host && *(volatile const unsigned *)comm->poison_host)
+        return xq4_fail(XQ4_ETIMEDOUT,
+                        "an earlier call on this communicator gave up waiting for a peer's rows (fault bit 0x8); "
+                        "the ranks' call counts are out of step: destroy and re-create the communicator");
+    return XQ4_OK;
+}
+
+namespace {
+void fill_poison(const xq4_comm *comm, xq4_p2p_poison *p)
+{
+    *p = xq4_p2p_poison{};
+    for (int q = 0; q < comm->nranks; q++) p->word[q] = (unsigned *)(comm->inbox.peer[q] + kPoisonOff);
+    p->host = comm->poison_dev;
+}
+}  // namespace
+
 int xq4_comm_chain_p2p(xq4_comm *comm, const xq4_device *dev, xq4_chain_p2p *out)
 {
     if (comm->dev != dev) return xq4_fail(XQ4_EINVAL, "communicator of another device");
@@ -388,6 +428,7 @@ int xq4_comm_chain_p2p(xq4_comm *comm, const xq4_device *dev, xq4_chain_p2p *out
         out->inbox[q] = (unsigned long long *)(comm->inbox.peer[q] + kInboxHead);
     out->half_words = XQ4_FUSED_MAX_VALUES;
     out->epoch = (unsigned *)(comm->inbox.local + 4);
+    fill_poison(comm, &out->poison);
     return XQ4_OK;
 }
 
@@ -412,6 +453,7 @@ extern "C" int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w, con
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
     if (!comm->inbox.local && comm->nranks > 1)
         if (int rc = setup_inbox(comm)) return rc;
+    if (int rc = xq4_comm_check_usable(comm)) return rc;
     xq4_p2p_out p{};
     p.nranks = comm->nranks;
     p.rank = comm->rank;
@@ -423,12 +465,16 @@ extern "C" int xq4_linear_sharded_fused(xq4_comm *comm, const xq4_weight *w, con
         p.half_words = XQ4_FUSED_MAX_VALUES;
         p.cnt = (unsigned *)comm->inbox.local;
         p.epoch = (unsigned *)(comm->inbox.local + 4);
+        fill_poison(comm, &p.poison);
         e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32,
                             (cudaStream_t)stream, &p);
     } else {  // one rank: the shard is the whole matrix
         e = xq4_launch_gemv(w->d_pack, w->n, w->k, x_dev, m, y_full_dev, out_dtype == XQ4_OUT_F32,
                             (cudaStream_t)stream);
     }
+    if (e == cudaErrorCooperativeLaunchTooLarge)
+        return xq4_fail(XQ4_ENOTSUP, "fused sharded launch: its CTAs wait for the peers' matching CTAs, so the whole "
+                                     "grid must be resident at once, and this device cannot hold it");
     if (e != cudaSuccess) return xq4_fail(XQ4_ECUDA, "fused sharded launch: %s", cudaGetErrorString(e));
     return XQ4_OK;
 }

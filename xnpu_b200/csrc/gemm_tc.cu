@@ -44,6 +44,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -471,7 +472,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 
 int sm_count()
 {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
@@ -523,7 +524,7 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {

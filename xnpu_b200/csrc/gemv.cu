@@ -50,9 +50,11 @@
 //  * Every mbarrier wait is bounded; a wait that runs out sets g_xq4_fault and
 //    the kernel returns.
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "xq4_internal.h"
 #include "xq4_layout.h"
@@ -270,6 +272,28 @@ __device__ __forceinline__ void pow2_split(int e, float &f1, float &f2)
     f2 = __int_as_float((e2 + 127) << 23);
 }
 
+// Poison a communicator whose peer wait ran out: this rank's word, every
+// peer's word and the host-mapped flag (idempotent plain stores).
+__device__ __forceinline__ void p2p_poison(const xq4_p2p_poison &p, int nranks)
+{
+    for (int q = 0; q < nranks; q++)
+        if (p.word[q]) xq4d::st_sys_u32(p.word[q], 1u);
+    if (p.host) xq4d::st_sys_u32(p.host, 1u);
+}
+
+// Lane 0 reads this rank's poison word and the warp agrees on it; a poisoned
+// communicator exchanges nothing, raises fault bit 0x8 and flags the host.
+__device__ __forceinline__ bool p2p_usable(const xq4_p2p_poison &p, int rank, int lane)
+{
+    unsigned v = lane == 0 ? xq4d::ld_sys_u32(p.word[rank]) : 0u;
+    v = __shfl_sync(0xffffffffu, v, 0);
+    if (v && lane == 0) {
+        atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+        if (p.host) xq4d::st_sys_u32(p.host, 1u);
+    }
+    return v == 0u;
+}
+
 template <int NT, bool XH, bool P2P>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
@@ -348,6 +372,8 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
         // completed before grid_dep_wait returned) and its inbox half
         const unsigned e = P2P ? *reinterpret_cast<volatile const unsigned *>(p2p.epoch) + 1u : 0u;
         const size_t half = P2P ? (size_t)(e & 1u) * p2p.half_words : 0;
+        // a poisoned communicator (an earlier call gave up on a peer): local rows only
+        const bool xchg = P2P && p2p_usable(p2p.poison, p2p.rank, lane);
         const float *red_c = red;
         bool alive = true;
         for (int rbl = 0; rbl < rb1 - rb0; rbl++) {
@@ -384,7 +410,7 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
                             bits = __bfloat16_as_ushort(h);
                         }
                         const unsigned long long word = ((unsigned long long)e << 32) | bits;
-                        for (int q = 0; q < p2p.nranks; q++)
+                        for (int q = 0; xchg && q < p2p.nranks; q++)
                             if (q != p2p.rank) xq4d::st_sys_u64(p2p.inbox[q] + half + idx, word);
                     } else if (out_f32) {
                         reinterpret_cast<float *>(y)[(size_t)tok * n + row] = sum;
@@ -405,7 +431,7 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             const unsigned long long *in = p2p.inbox[p2p.rank] + half;
             const int per_peer = m * span, total_w = (p2p.nranks - 1) * per_peer;
             const uint64_t t0 = xq4d::global_ns();
-            bool ok = alive;
+            bool ok = alive && xchg;
             for (int i = lane; ok && i < total_w; i += 32) {
                 const int qi = i / per_peer, rem = i - qi * per_peer;
                 const int tok = rem / span, row = r0 + (rem - tok * span);
@@ -422,6 +448,7 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
                 }
                 if (!ok) {
                     atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                    p2p_poison(p2p.poison, p2p.nranks);
                     break;
                 }
                 if (out_f32)
@@ -810,14 +837,18 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
         // inbox user on this stream completed before grid_dep_wait returned)
         const unsigned e = p2p.nranks > 1 ? *reinterpret_cast<volatile const unsigned *>(p2p.epoch) + 1u : 0u;
         const size_t half = p2p.nranks > 1 ? (size_t)(e & 1u) * p2p.half_words : 0;
+        // a poisoned communicator (an earlier call gave up on a peer): local rows only
+        const bool xchg = p2p.nranks > 1 && p2p_usable(p2p.poison, p2p.rank, lane);
         int rbl = 0, pend = 0;  // ops [pend, o] may hold sharded rows whose peer copies are not in y yet
         bool alive = true;
         for (int o = 0; o < n_ops; o++) {
             const xq4_chain_op_dev op = ops[o];
             int rb0, rb1;
             chain_range(op, cta, G, rb0, rb1);
-            const size_t ystride = op.shard ? (size_t)op.n_total : (size_t)op.n;
-            const int yoff = op.shard ? op.row_off : 0;
+            // output row stride and this rank's first output row (a SwiGLU op
+            // writes one value per row pair)
+            const size_t ystride = (size_t)(op.shard ? op.n_total : op.n) >> (op.swiglu ? 1 : 0);
+            const int yoff = op.shard ? (op.row_off >> (op.swiglu ? 1 : 0)) : 0;
             for (int rb = rb0; alive && rb < rb1; rb++, rbl++) {
                 const int buf = rbl % kRedBufs;
                 const uint32_t use = (uint32_t)(rbl / kRedBufs);
@@ -850,8 +881,15 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                         const float u = __shfl_xor_sync(0xffffffffu, hb, 1);
                         if (valid && !(r & 1)) {
                             const float gs = __fmul_rn(hb, __fdiv_rn(1.f, __fadd_rn(1.f, expf(-hb))));
-                            reinterpret_cast<__nv_bfloat16 *>(op.y)[(size_t)tok * (op.n >> 1) + (row >> 1)] =
-                                __float2bfloat16_rn(__fmul_rn(gs, u));
+                            const __nv_bfloat16 h = __float2bfloat16_rn(__fmul_rn(gs, u));
+                            const size_t idx = (size_t)tok * ystride + yoff + (row >> 1);
+                            reinterpret_cast<__nv_bfloat16 *>(op.y)[idx] = h;
+                            if (op.shard && xchg) {  // one word per peer (value bits + epoch)
+                                const unsigned long long word =
+                                    ((unsigned long long)e << 32) | (uint32_t)__bfloat16_as_ushort(h);
+                                for (int q = 0; q < p2p.nranks; q++)
+                                    if (q != p2p.rank) xq4d::st_sys_u64(p2p.inbox[q] + half + op.inbox_off + idx, word);
+                            }
                         }
                         continue;
                     }
@@ -874,7 +912,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                             reinterpret_cast<__nv_bfloat16 *>(op.y)[idx] = h;
                             bits = __bfloat16_as_ushort(h);
                         }
-                        if (op.shard) {  // one word per peer (value bits + epoch)
+                        if (op.shard && xchg) {  // one word per peer (value bits + epoch)
                             const unsigned long long word = ((unsigned long long)e << 32) | bits;
                             for (int q = 0; q < p2p.nranks; q++)
                                 if (q != p2p.rank) xq4d::st_sys_u64(p2p.inbox[q] + half + op.inbox_off + idx, word);
@@ -889,7 +927,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
             // from the inbox into y.  Each peer's CTA with this index
             // computed them (equal shards, equal chains), and every CTA sends
             // its words before it waits, so no wait depends on a waiting CTA.
-            if (p2p.nranks > 1 && (o + 1 == n_ops || ops[o + 1].wait_prev)) {
+            if (xchg && (o + 1 == n_ops || ops[o + 1].wait_prev)) {
                 const uint64_t t0 = xq4d::global_ns();
                 bool ok = alive;
                 for (int s = pend; ok && s <= o; s++) {
@@ -897,15 +935,20 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                     if (!so.shard) continue;
                     int s0, s1;
                     chain_range(so, cta, G, s0, s1);
-                    const int r0 = s0 * XQ4G_ROWS, span = min(s1 * XQ4G_ROWS, so.n) - r0;
+                    // this CTA's output rows of the op (row pairs for SwiGLU;
+                    // row blocks hold 16 rows, so a range never splits a pair)
+                    const int sh = so.swiglu ? 1 : 0;
+                    const int r0 = (s0 * XQ4G_ROWS) >> sh, span = (min(s1 * XQ4G_ROWS, so.n) >> sh) - r0;
                     if (span <= 0) continue;
+                    const int ns = so.n >> sh;
+                    const size_t stride = (size_t)so.n_total >> sh;
                     const unsigned long long *in = p2p.inbox[p2p.rank] + half + so.inbox_off;
                     const int per_peer = so.m * span, total_w = (p2p.nranks - 1) * per_peer;
                     for (int i = lane; ok && i < total_w; i += 32) {
                         const int qi = i / per_peer, rem = i - qi * per_peer;
                         const int tok = rem / span, row = r0 + (rem - tok * span);
                         const int q = qi < p2p.rank ? qi : qi + 1;
-                        const size_t idx = (size_t)tok * so.n_total + (size_t)q * so.n + row;
+                        const size_t idx = (size_t)tok * stride + (size_t)q * ns + row;
                         unsigned long long v = xq4d::ld_sys_u64(in + idx);
                         while ((unsigned)(v >> 32) != e) {
                             if (xq4d::global_ns() - t0 > 2000000000ull) {
@@ -917,6 +960,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                         }
                         if (!ok) {
                             atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                            p2p_poison(p2p.poison, p2p.nranks);
                             break;
                         }
                         if (so.out_f32)
@@ -1024,7 +1068,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
 
 int sm_count_of_current_device()
 {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
@@ -1036,11 +1080,28 @@ int sm_count_of_current_device()
     return cache[dev];
 }
 
+// Kernels whose CTAs wait for one another (the fused gather's peer waits,
+// the chain's op waits) need their whole grid resident at once; the bounded
+// waits would otherwise run out and leave wrong outputs behind a fault bit.
+// XQ4_RESIDENT_CTAS_PER_SM (environment, diagnostics) replaces the occupancy
+// query's answer, to emulate SMs held by another context.
+bool whole_grid_resident(const void *kernel, int threads, size_t smem, int grid)
+{
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (const char *f = getenv("XQ4_RESIDENT_CTAS_PER_SM"))
+        if (*f) per_sm = atoi(f);
+    return (long long)per_sm * sm_count_of_current_device() >= grid;
+}
+
 template <int NT, bool XH, bool P2P>
 cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int m, void *y, int out_f32,
                        cudaStream_t st, const xq4_p2p_out &p2p)
 {
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
@@ -1053,6 +1114,8 @@ cudaError_t launch_one(const uint8_t *pack, int n, int k, const uint16_t *x, int
     if (smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;  // never for the paths chosen below
     const int sms = sm_count_of_current_device();
     const int grid = nb < sms * kCtasPerSm ? nb : sms * kCtasPerSm;
+    if (P2P && p2p.nranks > 1 && !whole_grid_resident((const void *)gemv_kernel<NT, XH, P2P>, kThreads, smem, grid))
+        return cudaErrorCooperativeLaunchTooLarge;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
@@ -1105,6 +1168,24 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 
 size_t xq4_gemv_chain_smem() { return kChainSmem; }
 
+// Set the chain kernel's shared-memory attribute on the current device and
+// check that its whole grid can be resident (its op waits need that).
+cudaError_t xq4_gemv_chain_prepare()
+{
+    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmem);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    if (!whole_grid_resident((const void *)gemv_chain_kernel, kThreads, kChainSmem,
+                             sm_count_of_current_device() * kCtasPerSm))
+        return cudaErrorCooperativeLaunchTooLarge;
+    return cudaSuccess;
+}
+
 cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done,
                                   const xq4_chain_prep_dev *preps, int n_preps, const xq4_chain_p2p &p2p,
                                   cudaStream_t st)
@@ -1122,7 +1203,7 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
         cudaError_t e = cudaLaunchKernelEx(&pc, chain_prep_kernel, preps);
         if (e != cudaSuccess) return e;
     }
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
@@ -1131,7 +1212,8 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
         attr_set[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sm_count_of_current_device() * kCtasPerSm);  // every CTA resident (the op waits need it)
+    // every CTA resident (the op waits need it; checked at chain create)
+    cfg.gridDim = dim3(sm_count_of_current_device() * kCtasPerSm);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kChainSmem;
     cfg.stream = st;

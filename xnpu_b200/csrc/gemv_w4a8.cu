@@ -27,6 +27,7 @@
 // (0, 2, 1, 3) within each 4.  The staged activations are stored with the
 // same byte order (one prmt per word), so A and B agree slot by slot.
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -317,7 +318,7 @@ w4a8_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n, co
 
 int sm_count()
 {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
@@ -349,7 +350,7 @@ size_t xq4_w4a8_smem_bytes(int m, int k) { return smem_bytes(m < kMaxTok ? m : k
 cudaError_t xq4_launch_w4a8(const uint8_t *pack, int n, int k, const void *qx, const void *dx, int m, void *y,
                             int out_f32, cudaStream_t st)
 {
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {

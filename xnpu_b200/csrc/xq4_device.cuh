@@ -330,6 +330,16 @@ __device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long lon
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void st_sys_u32(unsigned *p, unsigned v)
+{
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_sys_u32(const unsigned *p)
+{
+    unsigned v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 // Bounded wait: false if the phase did not complete within about 2 s.  A
 // waiting thread is suspended in the barrier (up to 20 us per try) instead of
 // spinning, so it leaves the issue slots to the warps doing the work.

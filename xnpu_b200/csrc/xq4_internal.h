@@ -29,7 +29,20 @@ int xq4_repack_rows(const void *src, size_t src_len, const xq4_layout_desc *desc
 // halves used by epoch parity: no rank gets more than one call ahead of
 // another (a call ends only after the peers' words of that call arrived), so a
 // half is never rewritten while a rank still reads it.
+//
+// A peer wait that runs out leaves the ranks' epochs out of step for good (the
+// rank that gave up has advanced its epoch, its peers have not), after which a
+// later call could accept a word of another call whose tag happens to match.
+// So the kernel that gives up poisons the communicator: it sets the poison
+// word in its own inbox header and in every peer's, and the host-mapped flag
+// the host checks before each call.  A kernel that starts on a poisoned
+// communicator skips the exchange (it writes its own rows only), raises fault
+// bit 0x8 and sets the host flag; the host refuses further calls.
 #define XQ4_MAX_RANKS 8
+struct xq4_p2p_poison {
+    unsigned *word[XQ4_MAX_RANKS];  // rank q's poison word (peer-mapped; [rank] is local)
+    unsigned *host;                 // device address of the host-mapped flag
+};
 struct xq4_p2p_out {
     int nranks, rank;
     int n_total;                                // rows of the full output (n x nranks)
@@ -38,6 +51,7 @@ struct xq4_p2p_out {
     size_t half_words;                          // words per parity half (>= m x n_total)
     unsigned *cnt;                              // local: CTAs of the current launch that are done
     unsigned *epoch;                            // local: fused calls this rank has completed
+    xq4_p2p_poison poison;
 };
 
 // 64-K chunks per ring stage of the GEMV kernels (gemv.cu checks it).
@@ -66,8 +80,9 @@ struct xq4_chain_op_dev {
     int shard;
     int n_total, row_off;
     long long inbox_off;  // the op's first word in an inbox half
-    // Epilogues (not with shard): y = RNE(RNE(Wx) + residual), or SwiGLU of
-    // the row pairs (2i, 2i+1) into y[tok][n/2].
+    // Epilogues: y = RNE(RNE(Wx) + residual) (not with shard), or SwiGLU of
+    // the row pairs (2i, 2i+1) into y[tok][n/2] (sharded: y[tok][n_total/2],
+    // this rank's pairs from row_off/2).
     const uint16_t *residual;
     int swiglu;
     int wait_parity;      // phase parity of the consumers' op barrier at this op (waiting ops before it, mod 2)
@@ -79,6 +94,7 @@ struct xq4_chain_p2p {
     unsigned long long *inbox[XQ4_MAX_RANKS];  // rank q's inbox (peer-mapped; [rank] is local)
     size_t half_words;
     unsigned *epoch;               // the communicator's inbox epoch (shared with the fused GEMV)
+    xq4_p2p_poison poison;
 };
 struct xq4_comm;
 // Map the communicator's inboxes if not done yet (collective) and describe
@@ -86,6 +102,10 @@ struct xq4_comm;
 int xq4_comm_chain_p2p(struct xq4_comm *comm, const struct xq4_device *dev, struct xq4_chain_p2p *out);
 int xq4_comm_nranks(const struct xq4_comm *comm);
 int xq4_comm_rank(const struct xq4_comm *comm);
+// XQ4_OK, or the status to return when an earlier call on the communicator
+// gave up waiting for a peer (the communicator is unusable from then on).
+int xq4_comm_check_usable(const struct xq4_comm *comm);
+
 
 // One activation the chain reads through the fp16 path, converted once per
 // run (before the chain's consumers start) by the prep kernel.
@@ -130,6 +150,9 @@ cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops,
                                   const struct xq4_chain_prep_dev *preps, int n_preps,
                                   const struct xq4_chain_p2p &p2p, cudaStream_t st);
 size_t xq4_gemv_chain_smem();
+// Set up the chain kernel on the current device; cudaErrorCooperativeLaunchTooLarge
+// when its grid (2 CTAs per SM) cannot all be resident at once.
+cudaError_t xq4_gemv_chain_prepare();
 cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st);
 cudaError_t xq4_launch_dequant(const uint8_t *pack, int n, int k, void *out, cudaStream_t st);
