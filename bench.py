@@ -2,34 +2,35 @@
 
 Workload (one step = one token): the Llama-3-8B-shaped decode linear set at
 batch 1 -- 32 layers x {QKV 4096->6144, O 4096->4096, gate+up 4096->2x14336,
-down 14336->4096} -- with independent seeded random int4 weights per layer (group 32, bf16 scales |N(0,0.02)|/7.5, zero point 8) and
-bf16 N(0,1) activations; each projection reads a fixed activation, as the
-reference's projection-stream benchmark does (crates/xnpu-cli/src/main.rs:
-2487-2499, :3288).  3.93 GB of weights per step, far above the 126 MB L2, so
-no flush is needed between steps.
+down 14336->4096} -- with independent seeded random int4 weights per layer
+(group 32, bf16 scales |N(0,0.02)|/7.5, zero point 8) and bf16 N(0,1)
+activations; each projection reads a fixed activation, as the reference's
+projection-stream benchmark does (crates/xnpu-cli/src/main.rs:2487-2499,
+:3288).  3.93 GB of weights per step, far above the 126 MB L2, so no flush is
+needed between steps.
 
 Gate and up are one fused "gateup" projection, as in the reference's own
 layer chain (crates/xnpu-cli/src/main.rs:2464, :2488: 4 GEMV shapes per
-layer, qkv / o / gateup / down); the weight bytes are those of the two.
+layer, qkv / o / gateup / down); the weight bytes are those of the two, and
+its SwiGLU (the FFN's next step, main.rs:4732-4745) is fused into its
+epilogue, so it writes the 14336-value intermediate.
 
-On one GPU the step is ONE launch of the GEMV chain kernel over the 128
-projections (xq4_chain_run, after a small kernel that prepares the fp16
-activation images; the ops are independent because each reads its fixed
-activation).  The same chain with every op waiting for the previous
-one (a real decode step's dependency order) and the 128 separate GEMV
-launches (one CUDA graph) are timed beside it (``other_step_forms_ms``).
+The step is ONE launch of the GEMV chain kernel over the 128 projections
+(xq4_chain_run, after a small kernel that prepares the fp16 activation
+images).  On N GPUs (torchrun, one process per GPU) the gate/up projection is
+column-sharded N ways and each rank's SwiGLU values reach the peers inside
+the chain kernel over NVLink peer memory; QKV, O and down are replicated.
+The token is the same at every N, so scaling is "strong".  The same chain
+with every op waiting for the previous one (a real decode step's dependency
+order) is timed beside it, and at N = 1 the 128 GEMVs as separate launches in
+one CUDA graph.
 
-On N GPUs (torchrun, one process per GPU) the FFN gateup projection is
-column-sharded N ways, with the all-gather inside the GEMV kernel over NVLink
-peer memory (xq4_linear_sharded_fused); QKV, O and down are replicated; the
-step is the 128 launches in one CUDA graph.  The step is the same token, so
-scaling is "strong".  The line also reports the lm_head 4096->128256 (f32 logits)
-sharded the same way.
-
-Metric: tokens/s (higher is better); GB/s of algorithmic bytes (packed codes
-+ scales + x + y) and its fraction of the measured HBM peak are in
-``roofline``.  ``--impl reference`` times the reference's CPU path (the C
-restatement in oracle/, all host threads) on a bounded row sample.
+Also reported: the lm_head 4096->128256 (f32 logits, sharded the same way),
+config 0 (one 4096x4096 GEMV over rotating copies), config 2 (the gate
+projection at m = 1..64), config 3 (prefill GEMM, m = 2048), the W4A8 parity
+mode, and the reference's CPU path timed in full on this host
+(``cpu_baseline``).  ``--impl reference`` times that CPU path as the
+reference arm, one whole token per step.
 """
 import argparse
 import json
@@ -47,20 +48,27 @@ sys.path.insert(0, str(ROOT))
 
 LAYERS = 32
 SHAPES = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gateup", 28672, 4096), ("down", 4096, 14336)]
-SHARDED = ("gateup",)  # column-sharded over ranks; the rest are replicas
-# DRAM bytes (read + write) per launch of each projection at one GPU, from
-#   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
-#       --clock-control none -k regex:gemv --csv python bench.py --layers 4 --steps 1
-#       --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
-# (every launch of the capture; the figures repeat to within 0.01 %).
-DRAM_PER_LAUNCH = {"qkv": 14231808, "o": 9512960, "gateup": 66216960, "down": 33126912}
-# DRAM bytes (read + write) of one chain launch (the whole 32-layer step), from
+SHARDED = ("gateup",)  # column-sharded over ranks, its SwiGLU intermediate gathered; the rest are replicas
+# DRAM bytes (read + write) per layer of one chain launch, from
 #   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #       --clock-control none -k regex:gemv_chain --csv python bench.py --layers 4
-#       --steps 1 --warmup 3 --skip-e2e --skip-lmhead --no-cpu-baseline
-# (a 4-layer chain; its bytes scaled by 8 = the ratio of algorithmic bytes).
-CHAIN_DRAM_PER_STEP = 3929139200
+#       --steps 1 --warmup 3 --skip-e2e --skip-lmhead --skip-configs --no-cpu-baseline
+# (a 4-layer chain's bytes / 4; every layer has the same shapes).
+CHAIN_DRAM_PER_LAYER = 3929139200 // 32
 LMHEAD = (128256, 4096)
+METRIC = "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)"
+DTYPE = "int4 weights (u4 codes, bf16 scales), bf16 x, f32 accumulate"
+DATA = "synthetic (seeded PCG64; random-init 8B-shaped weights)"
+
+
+def config_of(world):
+    return {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
+                        "gateup 4096x28672 with its SwiGLU epilogue, down 14336x4096), M=1",
+            "group": 32, "layers": LAYERS, "batch": 1,
+            "parallelism": ("single GPU" if world == 1 else
+                            f"gate/up column-sharded x{world}, SwiGLU intermediate gathered inside the chain "
+                            f"kernel over NVLink peer memory; qkv/o/down replicated"),
+            "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"}
 
 
 def algo_bytes(n, k, m=1, out_bytes=2):
@@ -123,76 +131,108 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_baseline(steps=1, budget_s=12.0):
-    """The reference's CPU path (oracle restatement of main.rs:2287-2296 over
-    the L1 layout, rows split over all host threads) on a row sample of one
-    layer's four projections; scaled to tokens/s of the 32-layer set."""
+def layer_seed(li, si):
+    return 1 + 1000 * li + si
+
+
+def l1_image(codes, scales, tsi):
+    """The reference's L1 tile layout (tools/w4_import.py:4-14,
+    crates/xnpu-cli/src/main.rs:2186-2252) of a weight given as packed code
+    and scale planes: rows run through the 8 columns in order, so the image
+    is, tile by tile (tsi consecutive rows), the tile's nibble rows then its
+    bf16 scale rows."""
+    n = codes.shape[0]
+    c = codes.reshape(n // tsi, -1)
+    sc = np.ascontiguousarray(scales.astype("<u2")).view(np.uint8).reshape(n // tsi, -1)
+    return np.concatenate([c, sc], axis=1).reshape(-1)
+
+
+def cpu_layers(layers, seed_base=1):
+    """Every layer's four projections in the L1 layout (the reference's CPU
+    path reads that layout), the same seeded weights as the GPU arm."""
+    from concurrent.futures import ThreadPoolExecutor
+    from xnpu_b200 import synth
+
+    def one(li, si):
+        name, n, k = SHAPES[si]
+        seed = layer_seed(li, si) if seed_base == 1 else seed_base + 1000 * li + si
+        tsi = 4 if name == "down" else 16  # crates/xnpu-cli/src/main.rs:2461-2466
+        return (n, k, tsi, l1_image(synth.synth_codes(n, k, seed), synth.synth_scales(n, k, seed), tsi))
+
+    with ThreadPoolExecutor(max_workers=4) as ex:
+        futs = [[ex.submit(one, li, si) for si in range(len(SHAPES))] for li in range(layers)]
+        return [[f.result() for f in row] for row in futs]
+
+
+def cpu_token(O, layers, xs, threads):
+    """One full token of the reference's CPU path: every row of every
+    projection of every layer, the oracle restatement of the sequential-f32
+    GEMV of crates/xnpu-cli/src/main.rs:2287-2296 over the L1 layout, rows
+    split over `threads` host threads.  Returns seconds."""
+    t0 = time.perf_counter()
+    for layer in layers:
+        for n, k, tsi, pack in layer:
+            O.gemv_l1(pack, n, k, tsi, xs[k], nthreads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(layers=None, tokens=3):
+    """The reference's CPU path timed in full on this host's cores: `tokens`
+    whole tokens (all rows of all 32 layers each), median."""
     from oracle import oracle as O
     from xnpu_b200 import synth
     threads = os.cpu_count() or 1
-    frac = 1.0 / 16  # rows sampled per projection
-    samples = []
-    for name, n, k in SHAPES:
-        rows = max(128, int(n * frac) // 128 * 128)
-        q = synth.unpack_codes_signed(synth.synth_codes(rows, k, 7))
-        s = synth.synth_scales(rows, k, 7)
-        tsi = 4 if name == "down" else 16
-        pack = O.l1_pack(q, s, tsi=tsi)
-        x = synth.synth_x(1, k, 7)
-        samples.append((n, k, rows, tsi, pack, x))
-    t_layer = []
-    t_end = time.time() + budget_s
-    for _ in range(max(1, steps)):
-        t = 0.0
-        for n, k, rows, tsi, pack, x in samples:
-            t0 = time.perf_counter()
-            O.gemv_l1(pack, rows, k, tsi, x, nthreads=threads)
-            t += (time.perf_counter() - t0) * (n / rows)
-        t_layer.append(t)
-        if time.time() > t_end:
-            break
-    tok_s = 1.0 / (np.median(t_layer) * LAYERS)
-    return {"value": tok_s, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"1/16 of the rows of each of the 4 projections of one layer (L1 layout, sequential "
-                      f"f32 per row), {len(t_layer)} timed pass(es), scaled to 32 layers",
-            "gbs": sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS * tok_s / 1e9}
+    layers = layers or cpu_layers(LAYERS)
+    xs = {k: synth.synth_x(1, k, 11 + k) for k in (4096, 14336)}
+    cpu_token(O, layers[:1], xs, threads)  # warm-up: page the first layer in
+    ts = [cpu_token(O, layers, xs, threads) for _ in range(tokens)]
+    t = float(np.median(ts))
+    return {"value": 1.0 / t, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{tokens} whole tokens (every row of the 4 projections of all {len(layers)} layers, L1 "
+                      f"layout, sequential f32 per row, rows split over {threads} threads), median; no extrapolation",
+            "gbs": sum(algo_bytes(n, k) for _, n, k in SHAPES) * len(layers) / t / 1e9,
+            "seconds_per_token": t}
 
 
 def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the path (the oracle port:
+    the reference's CPU code is Rust, which this image cannot build), on the
+    same workload, one whole token per step, all host threads; rank 0 only."""
     if rank != 0:
         return
-    from oracle import oracle as O  # noqa: F401  (builds the oracle if needed)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(steps=1, budget_s=30.0)
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = float(np.median(vals))
-    line = {"metric": "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)", "value": v,
+    from oracle import oracle as O
+    from xnpu_b200 import synth
+    threads = os.cpu_count() or 1
+    layers = cpu_layers(LAYERS)
+    xs = {k: synth.synth_x(1, k, 11 + k) for k in (4096, 14336)}
+    for _ in range(args.warmup):
+        cpu_token(O, layers, xs, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_token(O, layers, xs, threads)
+    t = (time.perf_counter() - t0) / args.steps
+    v = 1.0 / t
+    sample = (f"whole tokens: every row of qkv/o/gateup/down of all {LAYERS} layers per step (L1 layout, "
+              f"sequential f32 per row, rows split over {threads} threads); no extrapolation")
+    line = {"metric": METRIC, "value": v,
             "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 / v, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int4 weights, bf16 x, f32 accumulate", "data": "synthetic (seeded)",
-            "impl": "reference",
-            "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
-                                   "gateup 4096x28672, down 14336x4096), M=1", "group": 32},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
-                             "sample": r["sample"]},
+            "ms_per_step": 1e3 * t, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": DTYPE, "data": DATA, "impl": "reference", "config": config_of(world),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------- GPU arm
-def make_weights(dev, rank, world, seed_base=1):
-    """All 32 layers' weights; gateup rows sharded over ranks."""
+def make_weights(dev, rank, world, layers, seed_base=1):
+    """All layers' weights; the gate/up projection's rows sharded over ranks."""
     from concurrent.futures import ThreadPoolExecutor
     from xnpu_b200 import hal, synth
 
     def one(li, si):
         name, n, k = SHAPES[si]
         seed = seed_base + 1000 * li + si
-        codes = synth.synth_codes(n, k, seed)
-        scales = synth.synth_scales(n, k, seed)
-        src = synth.planes_bytes(codes, scales)
+        src = synth.planes_bytes(synth.synth_codes(n, k, seed), synth.synth_scales(n, k, seed))
         r0, r1 = 0, 0
         if world > 1 and name in SHARDED:
             r0, r1 = rank * n // world, (rank + 1) * n // world
@@ -200,7 +240,7 @@ def make_weights(dev, rank, world, seed_base=1):
 
     weights = []
     with ThreadPoolExecutor(max_workers=4) as ex:
-        for li in range(LAYERS):
+        for li in range(layers):
             futs = [ex.submit(one, li, si) for si in range(len(SHAPES))]
             layer = {}
             for si, f in enumerate(futs):
@@ -209,6 +249,56 @@ def make_weights(dev, rank, world, seed_base=1):
                 del src
             weights.append(layer)
     return weights
+
+
+def step_ops(weights, xs, ys, comm, wait_prev):
+    """The step's 128 ops: per layer qkv, o, gateup (+ SwiGLU; column-sharded
+    over `comm` when given), down, each reading its fixed activation."""
+    ops = []
+    for li, layer in enumerate(weights):
+        for name, n, k in SHAPES:
+            op = [layer[name], xs[k].data_ptr(), ys[li][name].data_ptr(), 1, 0, wait_prev]
+            if name in SHARDED:
+                op += [comm, {"swiglu": True}]
+            ops.append(tuple(op))
+    return ops
+
+
+def out_rows(name, n):
+    return n // 2 if name in SHARDED else n  # gate/up writes one SwiGLU value per row pair
+
+
+class Timer:
+    """CUDA events on `stream` around `steps` calls, bracketed by a barrier
+    and a synchronize; the max over ranks."""
+
+    def __init__(self, stream, world):
+        import torch
+        self.torch, self.stream, self.world = torch, stream, world
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def __call__(self, run_one, steps):
+        torch = self.torch
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        self.barrier()
+        ev0.record(self.stream)
+        with torch.cuda.stream(self.stream):
+            for i in range(steps):
+                run_one(i)
+        ev1.record(self.stream)
+        self.barrier()
+        t_ms = ev0.elapsed_time(ev1) / steps
+        if self.world > 1:
+            import torch.distributed as dist
+            tt = torch.tensor([t_ms], device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t_ms = float(tt.item())
+        return t_ms
 
 
 def main():
@@ -222,10 +312,14 @@ def main():
                     help="layers of the weight set (32 = the benchmark; fewer only for profiler captures)")
     ap.add_argument("--skip-e2e", action="store_true", help="profiler captures only")
     ap.add_argument("--skip-lmhead", action="store_true", help="profiler captures only")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="profiler captures only: no config 0/2/3 objects, no W4A8 or other step forms")
     ap.add_argument("--kernel-case", choices=["gemv", "gemm", "w4a8"],
                     help="profiler captures: one projection launched warmup+steps times on GPU 0 "
                          "(gemv and w4a8: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048)")
     ap.add_argument("--case-m", type=int, default=None, help="token count of --kernel-case")
+    ap.add_argument("--case-n", type=int, default=None, help="rows of --kernel-case")
+    ap.add_argument("--case-k", type=int, default=None, help="K of --kernel-case")
     args = ap.parse_args()
     if args.kernel_case:
         kernel_case(args)
@@ -253,7 +347,7 @@ def main():
     meta = dev.metadata()
     L = lib()
 
-    weights = make_weights(dev, rank, world)
+    weights = make_weights(dev, rank, world, LAYERS)
     comm = None
     if world > 1:
         import ctypes
@@ -267,163 +361,82 @@ def main():
         check(L.xq4_comm_init(dev.handle, rank, world, ctypes.addressof(uid), ctypes.byref(h)))
         comm = h
 
-    # activations / outputs (fixed per shape, as the reference's stream benchmark)
+    # activations (fixed per K, as the reference's stream benchmark) and one
+    # output per op
     xs = {k: torch.from_numpy(synth.synth_x(1, k, 11 + k).view(np.int16)).cuda().view(torch.bfloat16)
           for k in (4096, 14336)}
-    ys = {name: torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for name, n, _ in SHAPES}
+    ys = [{name: torch.empty((1, out_rows(name, n)), dtype=torch.bfloat16, device="cuda") for name, n, _ in SHAPES}
+          for _ in range(LAYERS)]
     stream = torch.cuda.Stream()
-    sp = stream.cuda_stream
+    timed = Timer(stream, world)
 
-    def step(st):
-        launches = 0
-        for layer in weights:
-            for name, n, k in SHAPES:
-                w = layer[name]
-                if comm is not None and name in SHARDED:
-                    check(L.xq4_linear_sharded_fused(comm, w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
-                else:
-                    check(L.xq4_linear_raw(w.handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, st))
-                launches += 1
-        return launches
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def timed(run_one, steps):
-        """Device time per step (ms, max over ranks) of `steps` calls of
-        run_one on `stream`, bracketed by barrier + synchronize."""
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        ev0.record(stream)
+    # The step: ONE chain launch (plus the activation prep kernel) over the
+    # 128 projections, independent ops (each reads its fixed activation, the
+    # reference's projection-stream benchmark, main.rs:2487-2499).  At N > 1
+    # the gate/up op is column-sharded and its SwiGLU intermediate reaches the
+    # peers inside the kernel over NVLink; the other projections are replicas.
+    chains = {wp: hal.Chain(dev, step_ops(weights, xs, ys, comm, wp)) for wp in (0, 1)}
+    for wp in (0, 1):
         with torch.cuda.stream(stream):
-            for _ in range(steps):
-                run_one()
-        ev1.record(stream)
-        barrier()
-        t_ms = ev0.elapsed_time(ev1) / steps
-        if world > 1:
-            tt = torch.tensor([t_ms], device="cuda")
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t_ms = float(tt.item())
-        return t_ms
-
-    # Separate launches: warm-up (eager), then one step captured into a CUDA
-    # graph (128 launches per token are too many to issue from the host at
-    # HBM speed).
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step(sp)
-    barrier()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        per_step = step(stream.cuda_stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            graph.replay()
-    barrier()
-
-    # One GPU: the step as ONE chain launch (xq4_chain_run).  Every
-    # projection reads its fixed activation (the reference's projection-stream
-    # benchmark, main.rs:2487-2499), so the ops are independent (wait_prev =
-    # 0); the same chain with every op waiting for the previous one (the
-    # dependency order of a real decode step) is timed beside it.
-    chains = {}
-    if world == 1:
-        for wp in (0, 1):
-            chains[wp] = hal.Chain(dev, [(layer[name], xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, wp)
-                                         for layer in weights for name, n, k in SHAPES])
-            with torch.cuda.stream(stream):
-                for _ in range(args.warmup):
-                    chains[wp].run(stream)
-        barrier()
-
-    # device-timed steps (inputs resident in HBM)
+            for _ in range(args.warmup):
+                chains[wp].run(stream)
+    timed.barrier()
     with ClockSampler(local) as clk:
-        if world == 1:
-            ms = timed(lambda: chains[0].run(stream), args.steps)
-            per_step = 2  # the activation prep kernel + the chain kernel
-        else:
-            ms = timed(graph.replay, args.steps)
+        ms = timed(lambda i: chains[0].run(stream), args.steps)
     clocks = clk.summary()
-    launches = per_step * args.steps
-    alt = {"separate_launches_graph_ms": timed(graph.replay, args.steps)}
-    if world == 1:
-        alt["chain_dependent_ms"] = timed(lambda: chains[1].run(stream), args.steps)
-    for c in chains.values():
-        c.destroy()
+    launches = 2 * args.steps  # the prep kernel + the chain kernel per step
+    alt = {"chain_dependent_ms": timed(lambda i: chains[1].run(stream), args.steps)}
 
-    # roofline: algorithmic bytes of the step's GEMVs (per GPU) over the
-    # timed region's duration
-    gpu_step_bytes = 0
-    for name, n, k in SHAPES:
-        ns = n // world if (world > 1 and name in SHARDED) else n
-        gpu_step_bytes += algo_bytes(ns, k) * LAYERS
+    # Dominant kernel's launch duration, measured live: the chain kernel's
+    # share is nearly all of the step (the prep is one small CTA per distinct
+    # activation); its roofline uses the step's algorithmic bytes.
+    gpu_step_bytes = step_bytes_per_gpu(world)
     achieved = gpu_step_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
 
-    # isolated single-launch durations per shape (events around each launch;
-    # includes launch latency) -- diagnostic detail only
-    per = {name: [] for name, _, _ in SHAPES}
-    evs = []
-    with torch.cuda.stream(stream):
-        for layer in weights[:8]:
-            for name, n, k in SHAPES:
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
-                b.record(stream)
-                evs.append((name, a, b))
-    torch.cuda.synchronize()
-    for name, a, b in evs:
-        per[name].append(a.elapsed_time(b))
-    del graph
+    sharded_parity = None
+    if world > 1:
+        sharded_parity = check_sharded_step(dev, weights, xs, ys, chains[0], stream, rank, world)
 
-    # end-to-end through the C ABI with host buffers (pinned), copies inside
+    if world == 1 and not args.skip_configs:
+        alt["separate_launches_graph_ms"] = separate_launch_graph(weights, xs, stream, timed, args)
+
     e2e = None if args.skip_e2e else e2e_run(dev, weights, comm, world, args)
+    for c in chains.values():
+        c.destroy()
 
-    # lm_head (sharded the same way), f32 logits
-    lm = None if args.skip_lmhead else lmhead_run(dev, rank, world, comm, L, stream)
+    lm = None if args.skip_lmhead else lmhead_run(dev, rank, world, comm, L, stream, timed)
+    configs = None
+    if world == 1 and not args.skip_configs:
+        configs = {"config0_gemv_4096x4096": config0_run(dev, stream, timed, peak),
+                   "config2_gate_batch_sweep": config2_run(dev, stream, timed, peak),
+                   "config3_prefill_gemm": config3_run(dev, stream, timed)}
+    w4a8 = None if (args.skip_configs or world > 1) else w4a8_run(weights, xs, stream, timed, args)
 
-    # W4A8 parity mode (the reference's NPU numerics) on the same step, 1 GPU
-    w4a8 = None if (args.skip_e2e or world > 1) else w4a8_run(weights, xs, stream, args)
-
-    step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
     if rank == 0:
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
         line = {
-            "metric": "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)",
+            "metric": METRIC,
             "value": 1e3 / ms, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int4 weights (u4 codes, bf16 scales), bf16 x, f32 accumulate",
-            "data": "synthetic (seeded PCG64; random-init 8B-shaped weights)",
-            "config": {"workload": "llama3-8b decode linear set, 32 layers x (qkv 4096x6144, o 4096x4096, "
-                                   "gateup 4096x28672, down 14336x4096), M=1",
-                       "group": 32, "layers": LAYERS, "batch": 1,
-                       "parallelism": "single GPU" if world == 1 else f"gateup column-sharded x{world}, rows gathered by the GEMV over NVLink peer memory; qkv/o/down replicated",
-                       "l2": "inputs 3.93 GB per step >> 126 MB L2 (no flush needed)"},
-            "gbs": step_bytes * (1e3 / ms) / 1e9,
-            "roofline": ({"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                          "frac": achieved / peak, "peak_kind": peak_kind,
-                          "kernel": "gemv_chain_kernel (the step's 128 GEMVs in one launch, m=1)",
-                          "traffic": (CHAIN_DRAM_PER_STEP * LAYERS / 32 if CHAIN_DRAM_PER_STEP else None),
-                          "traffic_unit": "bytes per launch (ncu, 4-layer chain scaled by bytes to 32 layers)",
-                          "algorithmic_bytes_per_launch": gpu_step_bytes,
-                          "region": "one chain launch per step"}
-                         if world == 1 else
-                         {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                          "frac": achieved / peak, "peak_kind": peak_kind,
-                          "kernel": "gemv_kernel<1> (decode GEMV, m=1)", "traffic": None,
-                          "algorithmic_bytes_per_launch": gpu_step_bytes / LAYERS / len(SHAPES),
-                          "region": "all GEMV launches of the timed steps (CUDA graph replays)"}),
-            "isolated_launch_us": {k: 1e3 * float(np.mean(v)) for k, v in per.items()},
+            "dtype": DTYPE, "data": DATA, "config": config_of(world),
+            "gbs": gpu_step_bytes * (1e3 / ms) / 1e9,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "kernel": "gemv_chain_kernel (the step's 128 GEMVs in one launch, m=1)",
+                         "traffic": (CHAIN_DRAM_PER_LAYER * LAYERS if world == 1 else None),
+                         "traffic_unit": "bytes per launch (ncu dram read+write of a 4-layer chain, "
+                                         "per layer x layers)",
+                         "algorithmic_bytes_per_launch": gpu_step_bytes,
+                         "region": "one chain launch (+ the activation prep) per step, CUDA events"},
             "other_step_forms_ms": alt,
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
             "lm_head": lm,
+            "configs": configs,
             "w4a8": w4a8,
+            "sharded_parity": sharded_parity,
             "device": meta["name"],
         }
         if cpu is not None:
@@ -440,54 +453,245 @@ def main():
         dist.destroy_process_group()
 
 
+def step_bytes_per_gpu(world):
+    """Algorithmic bytes of one step on one GPU: codes + scales of its weights,
+    x, and its outputs (the gate/up op writes one SwiGLU value per pair)."""
+    total = 0
+    for name, n, k in SHAPES:
+        ns = n // world if name in SHARDED else n
+        total += algo_bytes(ns, k, out_bytes=2) - ns * 2 + out_rows(name, ns) * 2
+    return total * LAYERS
+
+
+def check_sharded_step(dev, weights, xs, ys, chain, stream, rank, world):
+    """Per-rank parity of the sharded op: layer 0's gate/up (+ SwiGLU)
+    intermediate as gathered by the sharded chain, against the same op run
+    unsharded on the full weight on this rank (the same kernel arithmetic per
+    row, so the bits must agree)."""
+    import torch
+    from xnpu_b200 import hal, synth
+    name, n, k = next(sh for sh in SHAPES if sh[0] in SHARDED)
+    seed = layer_seed(0, [sh[0] for sh in SHAPES].index(name))
+    src = synth.planes_bytes(synth.synth_codes(n, k, seed), synth.synth_scales(n, k, seed))
+    full = hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k))
+    ref = torch.full((1, n // 2), float("nan"), dtype=torch.bfloat16, device="cuda")
+    one = hal.Chain(dev, [(full, xs[k].data_ptr(), ref.data_ptr(), 1, 0, 0, None, {"swiglu": True})])
+    with torch.cuda.stream(stream):
+        chain.run(stream)
+        one.run(stream)
+    torch.cuda.synchronize()
+    got = ys[0][name]
+    same = bool(torch.equal(got.view(torch.int16), ref.view(torch.int16)))
+    a, b = got.float(), ref.float()
+    err = (a - b).abs()
+    floor = 1e-2 * b.pow(2).mean().sqrt()
+    res = {"rank": rank, "op": f"layer 0 {name} {n}x{k} + SwiGLU, {n // world} rows per rank",
+           "bit_identical_to_unsharded": same,
+           "max_rel": float((err / torch.maximum(b.abs(), floor)).max().item()),
+           "mae": float(err.mean().item()), "fault_bits": dev.fault()}
+    one.destroy()
+    full.destroy()
+    import torch.distributed as dist
+    gathered = [None] * world
+    dist.all_gather_object(gathered, res)
+    return gathered
+
+
+def separate_launch_graph(weights, xs, stream, timed, args):
+    """The same 128 GEMVs (gate/up without the SwiGLU epilogue) as separate
+    launches captured in one CUDA graph: the form the chain replaces."""
+    import torch
+    from xnpu_b200 import lib
+    from xnpu_b200._lib import check
+    L = lib()
+    ys = {name: torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for name, n, _ in SHAPES}
+
+    def step(sp):
+        for layer in weights:
+            for name, n, k in SHAPES:
+                check(L.xq4_linear_raw(layer[name].handle, xs[k].data_ptr(), ys[name].data_ptr(), 1, 0, sp))
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+    ms = timed(lambda i: graph.replay(), args.steps)
+    del graph
+    return ms
+
+
+def rotating_weights(dev, n, k, copies, seed):
+    """`copies` imports of one seeded n x k weight (each its own HBM copy):
+    launches cycle through them so that no launch finds its weights in L2."""
+    from xnpu_b200 import hal, synth
+    src = synth.planes_bytes(synth.synth_codes(n, k, seed), synth.synth_scales(n, k, seed))
+    return [hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k)) for _ in range(copies)]
+
+
+def config0_run(dev, stream, timed, peak, copies=36, reps=144):
+    """Config 0: one decode GEMV, m = 1, 4096 -> 4096 (9.45 MB), timed over
+    36 rotating weight copies (340 MB, > 2x the 126 MB L2).
+      * burst: back-to-back xq4_linear_raw launches on one stream (the
+        reference's pipelined mode, crates/xnpu-cli/src/main.rs:2404-2431),
+        CUDA events around all of them;
+      * sequential: one launch between two events and a synchronize, each;
+      * chained: the 36 GEMVs as one chain launch (xq4_chain_run)."""
+    import torch
+    from xnpu_b200 import hal, lib, synth
+    from xnpu_b200._lib import check
+    L = lib()
+    n, k = 4096, 4096
+    ws = rotating_weights(dev, n, k, copies, 1001)
+    x = torch.from_numpy(synth.synth_x(1, k, 1002).view(np.int16)).cuda().view(torch.bfloat16)
+    y = torch.empty((1, n), dtype=torch.bfloat16, device="cuda")
+    sp = stream.cuda_stream
+
+    def go(i):
+        check(L.xq4_linear_raw(ws[i % copies].handle, x.data_ptr(), y.data_ptr(), 1, 0, sp))
+
+    with torch.cuda.stream(stream):
+        for i in range(2 * copies):
+            go(i)
+    burst_us = 1e3 * timed(go, reps)
+    seq = []
+    for i in range(copies):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        with torch.cuda.stream(stream):
+            go(i)
+        b.record(stream)
+        b.synchronize()
+        seq.append(a.elapsed_time(b))
+    ys = [torch.empty((1, n), dtype=torch.bfloat16, device="cuda") for _ in range(copies)]
+    chain = hal.Chain(dev, [(w, x.data_ptr(), yy.data_ptr(), 1, 0, 0) for w, yy in zip(ws, ys)])
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            chain.run(stream)
+    chain_us = 1e3 * timed(lambda i: chain.run(stream), 8) / copies
+    chain.destroy()
+    for w in ws:
+        w.destroy()
+    b = algo_bytes(n, k)
+    gbs = b / (burst_us * 1e-6) / 1e9
+    return {"shape": "m=1, k=4096, n=4096", "algorithmic_bytes": b, "copies": copies,
+            "l2": f"{copies} rotating weight copies = {copies * b / 1e6:.0f} MB > 2x 126 MB L2",
+            "burst_us_per_gemv": burst_us, "sequential_us_per_gemv": 1e3 * float(np.median(seq)),
+            "chained_us_per_gemv": chain_us,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "region": "burst: back-to-back launches, events around all"},
+            "chained_gbs": b / (chain_us * 1e-6) / 1e9}
+
+
+def config2_run(dev, stream, timed, peak, copies=8, reps=48):
+    """Config 2: the gate projection 4096 -> 14336 (33 MB) at m in {1, 2, 4,
+    8, 16, 32, 64} through xq4_linear (decode GEMV below m = 25, tcgen05 GEMM
+    from m = 25), back-to-back launches over 8 rotating copies (264 MB)."""
+    import json as _json
+    import torch
+    from xnpu_b200 import lib, synth
+    from xnpu_b200._lib import check
+    L = lib()
+    tflops_peak = _json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops", 1590.0) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    n, k = 14336, 4096
+    ws = rotating_weights(dev, n, k, copies, 2001)
+    sp = stream.cuda_stream
+    out = {}
+    for m in (1, 2, 4, 8, 16, 32, 64):
+        x = torch.from_numpy(synth.synth_x(m, k, 2002 + m).view(np.int16)).cuda().view(torch.bfloat16)
+        y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+
+        def go(i):
+            check(L.xq4_linear_raw(ws[i % copies].handle, x.data_ptr(), y.data_ptr(), m, 0, sp))
+
+        with torch.cuda.stream(stream):
+            for i in range(copies):
+                go(i)
+        us = 1e3 * timed(go, reps)
+        b = algo_bytes(n, k, m)
+        gbs = b / (us * 1e-6) / 1e9
+        tfl = 2.0 * m * n * k / (us * 1e-6) / 1e12
+        out[str(m)] = {"us": us, "path": "gemv" if m < 25 else "tcgen05 gemm", "gbs": gbs,
+                       "hbm_frac": gbs / peak, "tflops": tfl, "tensor_frac": tfl / tflops_peak}
+    for w in ws:
+        w.destroy()
+    return {"shape": "k=4096, n=14336", "copies": copies, "l2": f"{copies} rotating weight copies (264 MB)",
+            "peaks": {"hbm_gbs": peak, "bf16_tflops": tflops_peak}, "by_m": out}
+
+
+def config3_run(dev, stream, timed, copies=3, reps=12):
+    """Config 3: prefill m = 2048, 4096 -> 14336, bf16 out, tcgen05 GEMM;
+    3 rotating weight and activation copies (150 MB of inputs)."""
+    import json as _json
+    import torch
+    from xnpu_b200 import lib, synth
+    from xnpu_b200._lib import check
+    L = lib()
+    pk = _json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    burst, sustained = pk.get("bf16_tflops", 1590.0), pk.get("bf16_tflops_sustained", 1400.0)
+    n, k, m = 14336, 4096, 2048
+    ws = rotating_weights(dev, n, k, copies, 3001)
+    xs = [torch.from_numpy(synth.synth_x(m, k, 3002 + i).view(np.int16)).cuda().view(torch.bfloat16)
+          for i in range(copies)]
+    y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    sp = stream.cuda_stream
+
+    def go(i):
+        check(L.xq4_linear_raw(ws[i % copies].handle, xs[i % copies].data_ptr(), y.data_ptr(), m, 0, sp))
+
+    with torch.cuda.stream(stream):
+        for i in range(2 * copies):
+            go(i)
+    us = 1e3 * timed(go, reps)
+    for w in ws:
+        w.destroy()
+    fl = 2.0 * m * n * k
+    tf = fl / (us * 1e-6) / 1e12
+    return {"shape": "m=2048, k=4096, n=14336", "flops": fl, "us": us,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": burst, "unit": "TFLOP/s", "frac": tf / burst,
+                         "peak_kind": "measured burst (cuBLAS bf16)", "frac_of_sustained": tf / sustained}}
+
+
 def e2e_run(dev, weights, comm, world, args):
-    """Same step through the public C ABI with host buffers: one pinned H2D of
-    the step's activations, 128 xq4_linear submits on the device queue, one
-    D2H of every output, xq4_wait -- timed on the host clock."""
+    """The same step through the public C ABI with host buffers: one pinned
+    H2D of the step's activations, one xq4_chain_submit of the 128 ops on
+    the device queue, xq4_wait, one D2H of every output -- timed on the host
+    clock, max over ranks."""
     import ctypes
     import torch
     from xnpu_b200 import hal, lib, synth
     from xnpu_b200._lib import check
     L = lib()
-    # per step inputs: one x per distinct K (the reference's benchmark feeds a
-    # fixed activation per shape); outputs: every projection of every layer
     k_off = {4096: 0, 14336: 4096 * 2}
     x_bytes = (4096 + 14336) * 2
-    y_sizes = [(li, name, n) for li in range(LAYERS) for name, n, _ in SHAPES]
     y_off, off = {}, 0
-    for li, name, n in y_sizes:
-        y_off[(li, name)] = off
-        off += ((n * 2 + 255) // 256) * 256
+    for li in range(LAYERS):
+        for name, n, _ in SHAPES:
+            y_off[(li, name)] = off
+            off += ((out_rows(name, n) * 2 + 255) // 256) * 256
     y_bytes = off
     xb = hal.BufferObject.new(dev, x_bytes)
     yb = hal.BufferObject.new(dev, y_bytes)
     hx = torch.empty(x_bytes, dtype=torch.uint8).pin_memory()
     hy = torch.empty(y_bytes, dtype=torch.uint8).pin_memory()
     hx.numpy()[:] = synth.synth_x(1, x_bytes // 2, 5).reshape(-1).view(np.uint8)
-    seq = ctypes.c_uint64()
-
-    chain = None
-    if comm is None:  # one GPU: the step is one chain submit (ops independent, as the timed step)
-        chain = hal.Chain(dev, [(layer[name], xb.device_ptr() + k_off[k], yb.device_ptr() + y_off[(li, name)],
-                                 1, 0, 0) for li, layer in enumerate(weights) for name, n, k in SHAPES])
+    ops = []
+    for li, layer in enumerate(weights):
+        for name, n, k in SHAPES:
+            op = [layer[name], xb.device_ptr() + k_off[k], yb.device_ptr() + y_off[(li, name)], 1, 0, 0]
+            if name in SHARDED:
+                op += [comm, {"swiglu": True}]
+            ops.append(tuple(op))
+    chain = hal.Chain(dev, ops)
 
     def one():
         check(L.xq4_buffer_upload(xb.handle, hx.data_ptr(), 0, x_bytes))
-        if chain is not None:
-            chain.submit()
-            check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
-            check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
-            return
-        for li, layer in enumerate(weights):
-            for name, n, k in SHAPES:
-                if comm is not None and name in SHARDED:
-                    xp = xb.device_ptr() + k_off[k]
-                    yp = yb.device_ptr() + y_off[(li, name)]
-                    check(L.xq4_linear_sharded_fused(comm, layer[name].handle, xp, yp, 1, 0,
-                                                     dev.stream_handle()))
-                else:
-                    check(L.xq4_linear(dev.handle, layer[name].handle, xb.handle, k_off[k], yb.handle,
-                                       y_off[(li, name)], 1, 0, ctypes.byref(seq)))
+        chain.submit()
         check(L.xq4_wait(dev.handle, L.xq4_last_seq(dev.handle), 60_000_000_000))
         check(L.xq4_buffer_download(yb.handle, hy.data_ptr(), 0, y_bytes))
 
@@ -504,20 +708,17 @@ def e2e_run(dev, weights, comm, world, args):
         t = torch.tensor([dt], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    if chain is not None:
-        chain.destroy()
+    chain.destroy()
     xb.destroy()
     yb.destroy()
-    path = ("xq4_buffer_upload -> xq4_chain_submit (the step's 128 GEMVs) -> xq4_wait -> xq4_buffer_download "
-            "(pinned host buffers)" if chain is not None else
-            "xq4_buffer_upload -> 128 x xq4_linear (gateup: xq4_linear_sharded_fused) -> xq4_wait -> "
-            "xq4_buffer_download (pinned host buffers)")
     return {"value": 1.0 / dt, "unit": "tok/s", "h2d_bytes_per_step": x_bytes, "d2h_bytes_per_step": y_bytes,
-            "ms_per_step": dt * 1e3, "path": path}
+            "ms_per_step": dt * 1e3,
+            "path": "xq4_buffer_upload -> xq4_chain_submit (the step's 128 ops) -> xq4_wait -> "
+                    "xq4_buffer_download (pinned host buffers)"}
 
 
-def w4a8_run(weights, xs, stream, args):
-    """The decode step in the W4A8 parity mode: per projection, quantize its
+def w4a8_run(weights, xs, stream, timed, args):
+    """The step in the W4A8 parity mode: per projection, quantize its
     activation (xq4_quantize_x) and run the int8-activation GEMV
     (xq4_linear_w4a8); CUDA-graph replays timed with events."""
     import torch
@@ -546,15 +747,7 @@ def w4a8_run(weights, xs, stream, args):
     with torch.cuda.stream(stream):
         for _ in range(max(3, args.warmup)):
             g.replay()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.steps):
-            g.replay()
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
+    ms = timed(lambda i: g.replay(), args.steps)
     del g
     step_bytes = sum(algo_bytes(n, k) for _, n, k in SHAPES) * LAYERS
     return {"tok_s": 1e3 / ms, "ms_per_step": ms, "gbs": step_bytes / (ms * 1e-3) / 1e9,
@@ -562,23 +755,20 @@ def w4a8_run(weights, xs, stream, args):
             "path": "per projection: xq4_quantize_x + xq4_linear_w4a8 (int8 activations, bf16 2048-K partials)"}
 
 
-def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
+def lmhead_run(dev, rank, world, comm, L, stream, timed, reps=20):
     """lm_head 4096 -> 128256, f32 logits, rows sharded over ranks and
     gathered inside the GEMV over peer memory; 8 rotating weight copies
-    (>2x L2 at every N)."""
+    (>2x L2 at every N).  At N > 1 each rank also runs the full matrix once
+    and compares the gathered logits with it."""
     import torch
-    import torch.distributed as dist
     from xnpu_b200 import hal, synth
     from xnpu_b200._lib import check
     n, k = LMHEAD
     r0, r1 = rank * n // world, (rank + 1) * n // world
     copies = 8 if world == 1 else max(8, 2 * world)
-    codes = synth.synth_codes(n, k, 424242)
-    scales = synth.synth_scales(n, k, 424242)
-    src = synth.planes_bytes(codes, scales)
+    src = synth.planes_bytes(synth.synth_codes(n, k, 424242), synth.synth_scales(n, k, 424242))
     ws = [hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k, row_begin=r0, row_end=r1))
           for _ in range(copies)]
-    del src
     x = torch.from_numpy(synth.synth_x(1, k, 9).view(np.int16)).cuda().view(torch.bfloat16)
     y = torch.empty((1, n), dtype=torch.float32, device="cuda")
     sp = stream.cuda_stream
@@ -592,26 +782,27 @@ def lmhead_run(dev, rank, world, comm, L, stream, reps=20):
     with torch.cuda.stream(stream):
         for i in range(5):
             go(i)
+    ms = timed(go, reps)
+    parity = None
     if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    with torch.cuda.stream(stream):
-        for i in range(reps):
-            go(i)
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        full = hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k))
+        yf = torch.empty((1, n), dtype=torch.float32, device="cuda")
+        with torch.cuda.stream(stream):
+            go(0)
+            check(L.xq4_linear_raw(full.handle, x.data_ptr(), yf.data_ptr(), 1, 1, sp))
+        torch.cuda.synchronize()
+        err = (y - yf).abs()
+        floor = 1e-2 * yf.pow(2).mean().sqrt()
+        parity = {"rank": rank, "vs": "the unsharded lm_head GEMV on this rank",
+                  "max_rel": float((err / torch.maximum(yf.abs(), floor)).max().item()),
+                  "mae": float(err.mean().item()), "argmax_equal": int(y.argmax()) == int(yf.argmax())}
+        full.destroy()
+    del src
     for w in ws:
         w.destroy()
     shard_bytes = algo_bytes(r1 - r0, k, out_bytes=4)
     return {"us": ms * 1e3, "shard_rows": r1 - r0, "gbs_per_gpu": shard_bytes / (ms * 1e-3) / 1e9,
-            "logits_gather_bytes_in": (n - (r1 - r0)) * 4}
+            "logits_gather_bytes_in": (n - (r1 - r0)) * 4, "parity_rank0": parity}
 
 
 def kernel_case(args):
@@ -622,6 +813,8 @@ def kernel_case(args):
     from xnpu_b200._lib import check
     n, k, m = (14336, 4096, 2048) if args.kernel_case == "gemm" else (65536, 4096, 1)
     m = args.case_m or m
+    n = args.case_n or n
+    k = args.case_k or k
     dev = hal.Device.open(0)
     L = lib()
     w = hal.Weight.import_(dev, synth.planes_bytes(synth.synth_codes(n, k, 31), synth.synth_scales(n, k, 31)),
