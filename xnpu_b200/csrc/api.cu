@@ -370,8 +370,10 @@ struct xq4_chain {
     int ordinal;
     int n_ops, n_preps;
     xq4_chain_op_dev *d_ops;  // one allocation: op table, n_ops + 1 completion counters,
-    unsigned *d_done;         // prep table, fp16 images
+    unsigned *d_done;         // prep table, range table, fp16 images
     xq4_chain_prep_dev *d_preps;
+    const int2 *d_rng;        // [op][cta] row-block ranges
+    int grid;                 // CTAs per launch (the range table's)
     xq4_chain_p2p p2p;        // sharded ops' communicator (nranks 1: none)
     xq4_comm *comm;           // that communicator, or NULL
 };
@@ -524,7 +526,26 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         op_prep[(size_t)i] = pi;
     }
     const size_t prep_bytes = align(preps.size() * sizeof(xq4_chain_prep_dev));
-    const size_t total = tab_bytes + done_bytes + prep_bytes + img_bytes;
+    // Row-block range of every op for every CTA: CTA c owns the row blocks
+    // whose first stage falls in [c*U/G, (c+1)*U/G) of its segment's U
+    // stages (shares differ by at most one row block).
+    const int grid = xq4_gemv_chain_grid();
+    std::vector<int2> rng((size_t)n_ops * grid);
+    for (int i = 0; i < n_ops; i++) {
+        const xq4_chain_op_dev &d = tab[(size_t)i];
+        const auto first_at = [&](long long st) -> int {  // first row block starting at stage >= st
+            if (st <= 0) return 0;
+            const long long r = (st + d.spr - 1) / d.spr;
+            return r < d.nb ? (int)r : d.nb;
+        };
+        for (int c = 0; c < grid; c++) {
+            const long long lo = (long long)c * d.seg_units / grid - d.seg_start;
+            const long long hi = (long long)(c + 1) * d.seg_units / grid - d.seg_start;
+            rng[(size_t)i * grid + c] = make_int2(first_at(lo), first_at(hi));
+        }
+    }
+    const size_t rng_bytes = align(rng.size() * sizeof(int2));
+    const size_t total = tab_bytes + done_bytes + prep_bytes + rng_bytes + img_bytes;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     void *mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, total);
@@ -532,7 +553,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         cudaGetLastError();
         return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the chain: %s", total, cudaGetErrorString(e));
     }
-    char *base = (char *)mem, *img = base + tab_bytes + done_bytes + prep_bytes;
+    char *base = (char *)mem, *rng_d = base + tab_bytes + done_bytes + prep_bytes, *img = rng_d + rng_bytes;
     std::vector<xq4_chain_prep_dev> ptab(preps.size());
     for (size_t q = 0; q < preps.size(); q++) {
         const prep_key &pk = preps[q];
@@ -554,6 +575,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     if (e == cudaSuccess && !ptab.empty())
         e = cudaMemcpy(base + tab_bytes + done_bytes, ptab.data(), ptab.size() * sizeof(xq4_chain_prep_dev),
                        cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(rng_d, rng.data(), rng.size() * sizeof(int2), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(mem);
@@ -561,8 +583,8 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     }
     xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
                                                 (unsigned *)(base + tab_bytes),
-                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes), p2p,
-                                                p2p.nranks > 1 ? comm : nullptr};
+                                                (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes),
+                                                (const int2 *)rng_d, grid, p2p, p2p.nranks > 1 ? comm : nullptr};
     if (!c) {
         cudaFree(mem);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -590,8 +612,8 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
     if (chain->comm)
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
-                             (cudaStream_t)stream),
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
+                             chain->n_preps, chain->p2p, (cudaStream_t)stream),
        "chain launch");
     return XQ4_OK;
 }
@@ -604,8 +626,8 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
     if (chain->comm)
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_done, chain->d_preps, chain->n_preps, chain->p2p,
-                             dev->stream),
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
+                             chain->n_preps, chain->p2p, dev->stream),
        "chain launch");
     const uint64_t s = dev->last_seq + 1;
     CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");

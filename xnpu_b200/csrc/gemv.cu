@@ -643,19 +643,16 @@ constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kStageBytes
 static_assert(kChainRingOff % 128 == 0, "ring alignment");
 static_assert((kChainSmem + 1024) * kCtasPerSm <= 228 * 1024, "kCtasPerSm chain CTAs per SM");
 
-// This CTA's row blocks of op `op`: those whose first stage falls in the
-// CTA's share [cta*U/G, (cta+1)*U/G) of its segment's U stages.
-__device__ __forceinline__ void chain_range(const xq4_chain_op_dev &op, int cta, int G, int &rb0, int &rb1)
+// This CTA's row blocks [rb0, rb1) of op o: those whose first stage falls in
+// the CTA's share [cta*U/G, (cta+1)*U/G) of its segment's U stages.  The host
+// computes the table at chain create (xq4_chain_ranges), one int2 per (op,
+// CTA): working it out here would cost every warp four 64-bit divisions per
+// op.
+__device__ __forceinline__ void chain_range(const int2 *__restrict__ rng, int o, int cta, int G, int &rb0, int &rb1)
 {
-    const long long lo = (long long)cta * op.seg_units / G - op.seg_start;
-    const long long hi = (long long)(cta + 1) * op.seg_units / G - op.seg_start;
-    const auto first_at = [&](long long s) -> int {  // first row block starting at stage >= s
-        if (s <= 0) return 0;
-        const long long r = (s + op.spr - 1) / op.spr;
-        return r < op.nb ? (int)r : op.nb;
-    };
-    rb0 = first_at(lo);
-    rb1 = first_at(hi);
+    const int2 r = __ldg(rng + (size_t)o * G + cta);
+    rb0 = r.x;
+    rb1 = r.y;
 }
 
 // Prep for the chain's fp16 path: one CTA per activation converts it as the
@@ -769,8 +766,8 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
 }
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned *__restrict__ done,
-                  const __grid_constant__ xq4_chain_p2p p2p)
+gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int2 *__restrict__ rng,
+                  unsigned *__restrict__ done, const __grid_constant__ xq4_chain_p2p p2p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -807,7 +804,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
             for (int o = 0; o < n_ops && alive; o++) {
                 const xq4_chain_op_dev op = ops[o];
                 int rb0, rb1;
-                chain_range(op, cta, G, rb0, rb1);
+                chain_range(rng, o, cta, G, rb0, rb1);
                 for (int rb = rb0; rb < rb1 && alive; rb++) {
                     for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks, i++) {
                         if (i >= kChainStages && !xq4d::mbar_wait(&empty[slot], phase ^ 1)) {
@@ -844,7 +841,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
         for (int o = 0; o < n_ops; o++) {
             const xq4_chain_op_dev op = ops[o];
             int rb0, rb1;
-            chain_range(op, cta, G, rb0, rb1);
+            chain_range(rng, o, cta, G, rb0, rb1);
             // output row stride and this rank's first output row (a SwiGLU op
             // writes one value per row pair)
             const size_t ystride = (size_t)(op.shard ? op.n_total : op.n) >> (op.swiglu ? 1 : 0);
@@ -934,7 +931,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
                     const xq4_chain_op_dev so = ops[s];
                     if (!so.shard) continue;
                     int s0, s1;
-                    chain_range(so, cta, G, s0, s1);
+                    chain_range(rng, s, cta, G, s0, s1);
                     // this CTA's output rows of the op (row pairs for SwiGLU;
                     // row blocks hold 16 rows, so a range never splits a pair)
                     const int sh = so.swiglu ? 1 : 0;
@@ -1017,7 +1014,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, unsigned 
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
                                              : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
         int rb0, rb1;
-        chain_range(op, cta, G, rb0, rb1);
+        chain_range(rng, o, cta, G, rb0, rb1);
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
         for (int rb = rb0; rb < rb1; rb++, rbl++) {
             for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {
@@ -1186,7 +1183,9 @@ cudaError_t xq4_gemv_chain_prepare()
     return cudaSuccess;
 }
 
-cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsigned *done,
+int xq4_gemv_chain_grid() { return sm_count_of_current_device() * kCtasPerSm; }
+
+cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid, unsigned *done,
                                   const xq4_chain_prep_dev *preps, int n_preps, const xq4_chain_p2p &p2p,
                                   cudaStream_t st)
 {
@@ -1212,8 +1211,9 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
         attr_set[dev] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    // every CTA resident (the op waits need it; checked at chain create)
-    cfg.gridDim = dim3(sm_count_of_current_device() * kCtasPerSm);
+    // every CTA resident (the op waits need it; checked at chain create); the
+    // grid the range table was built for
+    cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kChainSmem;
     cfg.stream = st;
@@ -1222,7 +1222,7 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, unsign
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, done, p2p);
+    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, rng, done, p2p);
 }
 
 // Read and clear this unit's fault word on the current device.

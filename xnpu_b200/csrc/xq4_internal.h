@@ -146,9 +146,13 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
                             const struct xq4_p2p_out *p2p = nullptr);
 // One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
 // n_ops + 1 zeroed counters (left zeroed at the end of the launch).
-cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, unsigned *done,
-                                  const struct xq4_chain_prep_dev *preps, int n_preps,
+// `rng` holds each op's row-block range per CTA ([op][cta], grid CTAs;
+// xq4_chain_ranges), built for `grid` = xq4_gemv_chain_grid() at create.
+cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid,
+                                  unsigned *done, const struct xq4_chain_prep_dev *preps, int n_preps,
                                   const struct xq4_chain_p2p &p2p, cudaStream_t st);
+// CTAs of a chain launch on the current device.
+int xq4_gemv_chain_grid();
 size_t xq4_gemv_chain_smem();
 // Set up the chain kernel on the current device; cudaErrorCooperativeLaunchTooLarge
 // when its grid (2 CTAs per SM) cannot all be resident at once.
