@@ -533,13 +533,15 @@ def rotating_weights(dev, n, k, copies, seed):
     return [hal.Weight.import_(dev, src, hal.layout_desc(hal.XQ4_LAYOUT_PLANES, n, k)) for _ in range(copies)]
 
 
-def config0_run(dev, stream, timed, peak, copies=36, reps=144):
+def config0_run(dev, stream, timed, peak, copies=36, reps=288):
     """Config 0: one decode GEMV, m = 1, 4096 -> 4096 (9.45 MB), timed over
     36 rotating weight copies (340 MB, > 2x the 126 MB L2).
-      * burst: back-to-back xq4_linear_raw launches on one stream (the
-        reference's pipelined mode, crates/xnpu-cli/src/main.rs:2404-2431),
-        CUDA events around all of them;
-      * sequential: one launch between two events and a synchronize, each;
+      * burst: back-to-back xq4_linear_raw launches, one per copy, captured
+        once in a CUDA graph and replayed (the reference's pipelined mode,
+        submit everything then drain, crates/xnpu-cli/src/main.rs:2404-2431),
+        CUDA events around the replays;
+      * sequential: submit one launch from the host and wait for it, each
+        (the reference's sequential mode), events around each;
       * chained: the 36 GEMVs as one chain launch (xq4_chain_run)."""
     import torch
     from xnpu_b200 import hal, lib, synth
@@ -557,7 +559,16 @@ def config0_run(dev, stream, timed, peak, copies=36, reps=144):
     with torch.cuda.stream(stream):
         for i in range(2 * copies):
             go(i)
-    burst_us = 1e3 * timed(go, reps)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(copies):
+            go(i)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+    burst_us = 1e3 * timed(lambda i: graph.replay(), reps // copies) / copies
+    del graph
     seq = []
     for i in range(copies):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -583,14 +594,15 @@ def config0_run(dev, stream, timed, peak, copies=36, reps=144):
             "burst_us_per_gemv": burst_us, "sequential_us_per_gemv": 1e3 * float(np.median(seq)),
             "chained_us_per_gemv": chain_us,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
-                         "region": "burst: back-to-back launches, events around all"},
+                         "region": "burst: 36 launches per CUDA graph replay, events around the replays"},
             "chained_gbs": b / (chain_us * 1e-6) / 1e9}
 
 
 def config2_run(dev, stream, timed, peak, copies=8, reps=48):
     """Config 2: the gate projection 4096 -> 14336 (33 MB) at m in {1, 2, 4,
     8, 16, 32, 64} through xq4_linear (decode GEMV below m = 25, tcgen05 GEMM
-    from m = 25), back-to-back launches over 8 rotating copies (264 MB)."""
+    from m = 25), back-to-back launches over 8 rotating copies (264 MB),
+    captured once in a CUDA graph and replayed."""
     import json as _json
     import torch
     from xnpu_b200 import lib, synth
@@ -612,7 +624,15 @@ def config2_run(dev, stream, timed, peak, copies=8, reps=48):
         with torch.cuda.stream(stream):
             for i in range(copies):
                 go(i)
-        us = 1e3 * timed(go, reps)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                go(i)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        us = 1e3 * timed(lambda i: graph.replay(), reps // copies) / copies
+        del graph
         b = algo_bytes(n, k, m)
         gbs = b / (us * 1e-6) / 1e9
         tfl = 2.0 * m * n * k / (us * 1e-6) / 1e12

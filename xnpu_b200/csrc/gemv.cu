@@ -140,7 +140,10 @@ __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
 // XG (fp16 path only): the fp16 activations and the correction table come
 // from global memory (xr = the prepared fp16 rows, tblg = the table) instead
 // of this CTA's shared-memory staging.
-template <int NT, bool SAFE, bool XH, bool COH = false, bool XG = false>
+// M1 (one token): only the MMA's column 0 -- token 0, in lanes t = 0 -- is
+// live, so each group's scale goes onto the two live accumulators (rows g and
+// g+8) with two plain FMAs instead of two packed pair FMAs over all four.
+template <int NT, bool SAFE, bool XH, bool COH = false, bool XG = false, bool M1 = false>
 __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, uint32_t phase, int kc0,
                                               int kc_n, int k, const uint16_t *const (&xr)[NT],
                                               const uint32_t (&xs)[NT], uint32_t tbl, int warp, int lane,
@@ -247,8 +250,13 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                         xq4d::mma_bf16_16816_z(tacc, a0, xf[c][nt][G2].x, xf[c][nt][G2].y);
                         xq4d::mma_bf16_16816(tacc, a1, xf[c][nt][G2].z, xf[c][nt][G2].w);
                     }
-                    xq4d::ffma2(acc[nt][0], acc[nt][1], s_lo, tacc[0], tacc[1]);
-                    xq4d::ffma2(acc[nt][2], acc[nt][3], s_hi, tacc[2], tacc[3]);
+                    if (M1) {
+                        acc[nt][0] = __fmaf_rn(s_lo, tacc[0], acc[nt][0]);
+                        acc[nt][2] = __fmaf_rn(s_hi, tacc[2], acc[nt][2]);
+                    } else {
+                        xq4d::ffma2(acc[nt][0], acc[nt][1], s_lo, tacc[0], tacc[1]);
+                        xq4d::ffma2(acc[nt][2], acc[nt][3], s_hi, tacc[2], tacc[3]);
+                    }
                 }
             }
         }
@@ -574,8 +582,15 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
     for (int i = 0; i < total; i++) {
         const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
         const bool fast = (XH || k_whole) && kc0 + kStageChunks <= kc_n;
-        const bool ok = fast ? consume_stage<NT, false, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc)
-                             : consume_stage<NT, true, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc);
+        bool ok;
+#ifndef XQ4_CHAIN_NO_M1
+        if (NT == 1 && m == 1 && fast)  // one token: the M1 form
+            ok = consume_stage<NT, false, XH, false, false, true>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s,
+                                                                  warp, lane, acc);
+        else
+#endif
+            ok = fast ? consume_stage<NT, false, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc)
+                      : consume_stage<NT, true, XH>(stage, &full[slot], phase, kc0, kc_n, k, xr, xs, tbl_s, warp, lane, acc);
         if (!ok) {
             atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
             return;
@@ -1021,6 +1036,12 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                 const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
                 const bool whole = kc0 + kStageChunks <= op.kc;
                 bool ok;
+#ifndef XQ4_CHAIN_NO_M1
+                if (op.xh && op.m == 1 && whole)  // one token, fp16 path, whole stage: the M1 form
+                    ok = consume_stage<1, false, true, false, true, true>(stage, &full[slot], phase, kc0, op.kc, op.k,
+                                                                         xr, xs, 0u, warp, lane, acc, op.xh_tbl);
+                else
+#endif
                 if (op.xh)  // fp16 path: K padding is zero in the image
                     ok = whole ? consume_stage<1, false, true, false, true>(stage, &full[slot], phase, kc0, op.kc, op.k,
                                                                            xr, xs, 0u, warp, lane, acc, op.xh_tbl)

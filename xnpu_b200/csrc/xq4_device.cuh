@@ -182,7 +182,13 @@ __device__ __forceinline__ void unpack_word_h16(uint32_t w, uint32_t (&a)[4])
 // through the MMA's accumulator input.
 __device__ __forceinline__ void unpack_word_c16(uint32_t w, uint32_t (&a)[4])
 {
+#ifdef XQ4_C16_SHIFT_IMAD
+    // w >> 8 as the high word of w * 2^24: an integer multiply-high, which
+    // issues to the FMA pipe and leaves the integer ALU pipe to the ANDs
+    const uint32_t w8 = __umulhi(w, 1u << 24);
+#else
     const uint32_t w8 = w >> 8;
+#endif
     a[0] = w & 0x000F000Fu;
     a[1] = w & 0x00F000F0u;
     a[2] = w8 & 0x000F000Fu;
