@@ -276,6 +276,36 @@ int xq4_quantize_x(const void *x_dev, int m, int k, void *q_dev, void *d_dev, in
 int xq4_linear_w4a8(const xq4_weight *w, const void *q_dev, const void *d_dev, void *y_dev, int m,
                     int out_dtype, void *stream);
 
+/* ---------------------------------------------------------------- decode attention */
+/* The attention side of a decode step, one launch per layer, standing in for
+ * the reference's host glue of its decode loop: rope_table + rope_apply
+ * (crates/xnpu-cli/src/main.rs:4817-4839), the per-head q/k RMSNorm
+ * qk_rms_bf16 (main.rs:4844-4857) and the GQA decode attention
+ * attention_bf16 (main.rs:4967-5033).  Head dim 128.  An xq4_attn holds the
+ * RoPE table (every position of the cache, computed on the host with the
+ * reference's f32 formula: base^(-j/64), cos/sin of pos * that), the split
+ * partials and the merge counters of one attention shape; calls on one
+ * xq4_attn must not overlap on the GPU (one stream). */
+typedef struct xq4_attn xq4_attn;
+/* heads q heads over nkv kv heads (heads % nkv == 0, at most 8 q heads per kv
+ * head), caches of cache_seq positions; rope_base 0 = no RoPE. */
+int xq4_attn_create(xq4_device *dev, int heads, int nkv, int cache_seq, float rope_base, xq4_attn **out);
+int xq4_attn_destroy(xq4_attn *attn);
+/* For the token at position *pos_dev (device int, 0 <= pos < cache_seq; read
+ * by the kernel, so a CUDA graph can replay the call as pos advances):
+ * qkv_dev bf16 [heads*128 | nkv*128 k | nkv*128 v] is the token's qkv
+ * projection output.  q and k are rotated by RoPE (one bf16 rounding) and,
+ * when q_norm_w_dev / k_norm_w_dev (bf16 [128], shared by the heads; NULL =
+ * none) are given, RMS-normalised per head; k and v are written into the
+ * caches (bf16 [nkv][cache_seq][128]) at pos; out_dev (bf16 [heads*128])
+ * receives, per q head h, softmax((K q_h) / sqrt(128)) . V over positions
+ * 0..pos of kv head h / (heads / nkv), in f32, rounded once.  qkv and the
+ * caches 16-byte aligned, out 8-byte aligned.  A position outside the cache
+ * writes nothing and sets fault bit 0x20 (xq4_device_fault).  Runs on
+ * `stream` (cudaStream_t; NULL = CUDA's default stream). */
+int xq4_attn_decode(xq4_attn *attn, const void *qkv_dev, const void *q_norm_w_dev, const void *k_norm_w_dev,
+                    void *k_cache_dev, void *v_cache_dev, const int *pos_dev, void *out_dev, void *stream);
+
 /* ---------------------------------------------------------------- shards */
 /* Column (N) sharding of large-N projections over P GPUs with an NCCL
  * all-gather of the outputs.  The reference is single-device; its nearest

@@ -117,6 +117,9 @@ SIGNATURES = {
     "xq4_linear_sharded_fused": (_I, [_P, _P, _P, _P, _I, _I, _P]),
     "xq4_quantize_x": (_I, [_P, _I, _I, _P, _P, _I, _P]),
     "xq4_linear_w4a8": (_I, [_P, _P, _P, _P, _I, _I, _P]),
+    "xq4_attn_create": (_I, [_P, _I, _I, _I, ctypes.c_float, _PP]),
+    "xq4_attn_destroy": (_I, [_P]),
+    "xq4_attn_decode": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

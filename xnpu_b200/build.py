@@ -14,7 +14,7 @@ CSRC = PKG / "csrc"
 OUT = PKG / "libxq4.so"
 BUILD = PKG / "_build"
 
-CU_SOURCES = ["api.cu", "gemv.cu", "gemv_w4a8.cu", "gemm_tc.cu", "dequant.cu", "comm.cu"]
+CU_SOURCES = ["api.cu", "gemv.cu", "gemv_w4a8.cu", "gemm_tc.cu", "dequant.cu", "comm.cu", "attn.cu"]
 CPP_SOURCES = ["repack.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

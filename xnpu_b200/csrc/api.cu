@@ -430,6 +430,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh = 0;
         d.xh_img = nullptr;
         d.xh_tbl = nullptr;
+        d.xh_tbl1 = nullptr;
         d.xh_max = nullptr;
         d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
         d.shard = o.comm && p2p.nranks > 1;
@@ -479,7 +480,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         int m, k;
         const void *norm_w;
         float eps;
-        size_t img_off, tbl_off, max_off;
+        size_t img_off, tbl_off, tbl1_off, max_off;
     };
     // bytes of op j's output
     const auto y_bytes = [&](int j) {
@@ -512,12 +513,14 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
                 preps[q].norm_w == o.norm_w_dev && (!o.norm_w_dev || preps[q].eps == o.norm_eps))
                 pi = (int)q;
         if (pi < 0) {
-            prep_key pk{o.x_dev, o.m, o.w->k, o.norm_w_dev, o.norm_eps, 0, 0, 0};
+            prep_key pk{o.x_dev, o.m, o.w->k, o.norm_w_dev, o.norm_eps, 0, 0, 0, 0};
             const size_t kp = (size_t)o.w->kc * XQ4G_KCHUNK;
             pk.img_off = img_bytes;
             img_bytes += align((size_t)o.m * kp * 2);
             pk.tbl_off = img_bytes;
             img_bytes += align((size_t)o.w->kc * 32 * sizeof(float));
+            pk.tbl1_off = img_bytes;
+            img_bytes += align((size_t)o.w->kc * 2 * sizeof(float4));
             pk.max_off = img_bytes;
             img_bytes += 256;
             pi = (int)preps.size();
@@ -558,6 +561,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     for (size_t q = 0; q < preps.size(); q++) {
         const prep_key &pk = preps[q];
         ptab[q] = xq4_chain_prep_dev{pk.x, (uint16_t *)(img + pk.img_off), (float *)(img + pk.tbl_off),
+                                     (float4 *)(img + pk.tbl1_off),
                                      (unsigned *)(img + pk.max_off), pk.m, pk.k, (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK,
                                      pk.norm_w != nullptr, (const uint16_t *)pk.norm_w, pk.eps, 0};
     }
@@ -568,6 +572,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh = 1;
         d.xh_img = ptab[(size_t)pi].img;
         d.xh_tbl = (const float4 *)ptab[(size_t)pi].tbl;
+        d.xh_tbl1 = ptab[(size_t)pi].tbl1;
         d.xh_max = ptab[(size_t)pi].max;
     }
     e = cudaMemcpy(base, tab.data(), tab.size() * sizeof(xq4_chain_op_dev), cudaMemcpyHostToDevice);
@@ -678,6 +683,6 @@ extern "C" int xq4_device_fault(xq4_device *dev, uint32_t *bits)
     if (!dev || !bits) return xq4_fail(XQ4_EINVAL, "NULL argument");
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     CK(cudaDeviceSynchronize(), "synchronize before reading the fault word");
-    *bits = xq4_take_fault_gemv() | xq4_take_fault_gemm() | xq4_take_fault_w4a8();
+    *bits = xq4_take_fault_gemv() | xq4_take_fault_gemm() | xq4_take_fault_w4a8() | xq4_take_fault_attn();
     return XQ4_OK;
 }

@@ -91,6 +91,7 @@ constexpr int kStages = XQ4_GEMV_STAGES;
 #endif
 constexpr int kCtasPerSm = XQ4_GEMV_CTAS_PER_SM;  // resident CTAs per SM (grid = SMs x this)
 constexpr int kStageBytes = kStageChunks * XQ4G_UNIT_BYTES;
+constexpr int kStageXBytes = kStageChunks * XQ4G_KCHUNK * 2;  // one token's fp16 x for a stage's chunks
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kProducerWarp = kConsumerWarps;     // one thread issues the bulk copies
 constexpr int kReducerWarp = kConsumerWarps + 1;  // sums the row blocks' partials, writes y
@@ -143,12 +144,17 @@ __host__ __device__ inline size_t smem_bytes(int nt, bool xh, int m, int kc_n)
 // M1 (one token): only the MMA's column 0 -- token 0, in lanes t = 0 -- is
 // live, so each group's scale goes onto the two live accumulators (rows g and
 // g+8) with two plain FMAs instead of two packed pair FMAs over all four.
-template <int NT, bool SAFE, bool XH, bool COH = false, bool XG = false, bool M1 = false>
+// XS (chain, one token, whole stage; implies XH, XG and M1): the stage holds,
+// after its weights, the chunks' fp16 activation slice and their one-token
+// zero-point entries ({z, z, 16 z, 16 z} per group, the MMA's accumulator
+// input as it stands); both are read from shared memory after the stage wait.
+template <int NT, bool SAFE, bool XH, bool COH = false, bool XG = false, bool M1 = false, bool XS = false>
 __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, uint32_t phase, int kc0,
                                               int kc_n, int k, const uint16_t *const (&xr)[NT],
                                               const uint32_t (&xs)[NT], uint32_t tbl, int warp, int lane,
                                               float (&acc)[NT][4], const float4 *tblg = nullptr)
 {
+    static_assert(!XS || (NT == 1 && !SAFE && XH && XG && M1), "XS: one token, whole stage, fp16 path");
     // chunks whose activation runs are held in registers at once (bounds
     // the register file for 16-token tiles)
     constexpr int R = NT == 1 ? kChunksInFlight : 2;
@@ -156,6 +162,7 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
 #pragma unroll
     for (int c0 = 0; c0 < kCpw; c0 += R) {
         uint4 xf[R][NT][2];  // 8 K of group 0 and 8 K of group 1, per chunk
+        if (XS && c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
 #pragma unroll
         for (int c = 0; c < R; c++) {
             const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
@@ -164,7 +171,10 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
 #pragma unroll
                 for (int G2 = 0; G2 < 2; G2++) {
                     const int kb = kc * XQ4G_KCHUNK + 32 * G2 + 8 * t;
-                    if (XH && XG) {
+                    if (XS) {
+                        const int cl = warp + (c0 + c) * kConsumerWarps;  // chunk within the stage
+                        xf[c][nt][G2] = xq4d::lds_v4(stage + kStageBytes + 2 * (cl * XQ4G_KCHUNK + 32 * G2 + 8 * t));
+                    } else if (XH && XG) {
                         xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::ldg_v4(xr[nt] + kb) : make_uint4(0, 0, 0, 0);
                     } else if (XH) {
                         xf[c][nt][G2] = (!SAFE || kc < kc_n) ? xq4d::lds_v4(xs[nt] + 2 * kb)
@@ -176,7 +186,7 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
                     }
                 }
         }
-        if (c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
+        if (!XS && c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
         // fp16 path: zero-point corrections of the chunk's two groups; from
         // the prepared table (XG) they are the MMA's accumulator inputs as
         // they stand, {z(2t), z(2t+1), 16 z(2t), 16 z(2t+1)} per group
@@ -186,7 +196,11 @@ __device__ __forceinline__ bool consume_stage(uint32_t stage, uint64_t *full, ui
             for (int c = 0; c < R; c++) {
                 const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
                 const bool in = !SAFE || kc < kc_n;
-                if (XG) {
+                if (XS) {
+                    const int cl = warp + (c0 + c) * kConsumerWarps;
+                    zc[c][0] = xq4d::lds_f4(stage + kStageBytes + kStageXBytes + 32 * cl);
+                    zc[c][1] = xq4d::lds_f4(stage + kStageBytes + kStageXBytes + 32 * cl + 16);
+                } else if (XG) {
                     zc[c][0] = in ? xq4d::ldg_f4(tblg + (kc * 4 + t) * 2) : make_float4(0.f, 0.f, 0.f, 0.f);
                     zc[c][1] = in ? xq4d::ldg_f4(tblg + (kc * 4 + t) * 2 + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
                 } else {
@@ -651,10 +665,19 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 #endif
 constexpr int kChainStages = XQ4_CHAIN_STAGES;
 static_assert(kStageChunks == XQ4_GEMV_STAGE_CHUNKS_ABI, "the host splits chain work in these stages");
+// A chain stage: the weights of kStageChunks chunks, then, for a one-token
+// fp16-path op, the slices of its activation image (kStageChunks * 64 fp16)
+// and of its one-token zero-point table (kStageChunks * 2 float4) that those
+// chunks read -- copied in by the same bulk-copy engine, so that the
+// consumers' hot loop reads shared memory only.
+constexpr int kChainXBytes = kStageXBytes;
+constexpr int kChainTBytes = kStageChunks * 2 * 16;
+constexpr int kChainStageBytes = kStageBytes + kChainXBytes + kChainTBytes;
 // ring full/empty, reduce full/free, and the consumers' op barrier
 constexpr int kChainBarBytes = ((2 * kChainStages + 2 * kRedBufs + 1) * 8 + 127) & ~127;
 constexpr size_t kChainRingOff = kChainBarBytes + (size_t)kRedBufs * kConsumerWarps * 128 * 4;
-constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kStageBytes;
+constexpr size_t kChainSmem = kChainRingOff + (size_t)kChainStages * kChainStageBytes;
+static_assert(kChainStageBytes % 128 == 0, "stage alignment");
 static_assert(kChainRingOff % 128 == 0, "ring alignment");
 static_assert((kChainSmem + 1024) * kCtasPerSm <= 228 * 1024, "kCtasPerSm chain CTAs per SM");
 
@@ -690,6 +713,8 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     __shared__ float sinv[8];
     if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
     for (int i = threadIdx.x; i < p.kc * 32; i += kPrepThreads) p.tbl[i] = 0.f;
+    if (p.m == 1)  // a half chunk's missing group keeps a zero entry
+        for (int i = threadIdx.x; i < p.kc * 2; i += kPrepThreads) p.tbl1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (p.norm) {
         // RMSNorm (crates/xnpu-cli/src/main.rs:4714-4724): warp w sums the
         // squares of token w, lane-strided then a fixed butterfly, so the
@@ -772,6 +797,7 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
             float *e = p.tbl + (((grp >> 1) * 4 + (tok >> 1)) * 2 + (grp & 1)) * 4 + (tok & 1);
             e[0] = z;
             e[2] = 16.f * z;
+            if (p.m == 1) p.tbl1[grp] = make_float4(z, z, 16.f * z, 16.f * z);  // [chunk][group]
         }
     }
     const int pad_runs = (kp - p.k) / 8;  // k % 64 == 32: one half chunk per token
@@ -816,6 +842,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
             int slot = 0, i = 0;
             uint32_t phase = 0;
             bool alive = true;
+            bool prep_done = false;  // the x and table slices are the prep kernel's output
             for (int o = 0; o < n_ops && alive; o++) {
                 const xq4_chain_op_dev op = ops[o];
                 int rb0, rb1;
@@ -829,9 +856,21 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                         }
                         const int cnt = min(kStageChunks, op.kc - kc0);
                         const uint32_t bytes = (uint32_t)cnt * XQ4G_UNIT_BYTES;
-                        xq4d::mbar_arrive_expect_tx(&full[slot], bytes);
-                        xq4d::bulk_g2s(ring + (size_t)slot * kStageBytes,
-                                       op.pack + ((size_t)rb * op.kc + kc0) * XQ4G_UNIT_BYTES, bytes, &full[slot]);
+                        // one-token fp16 op, whole stage: its x and table slices come along
+                        const bool xs = op.xh && op.m == 1 && cnt == kStageChunks;
+                        uint8_t *dst = ring + (size_t)slot * kChainStageBytes;
+                        xq4d::mbar_arrive_expect_tx(&full[slot], bytes + (xs ? kChainXBytes + kChainTBytes : 0));
+                        xq4d::bulk_g2s(dst, op.pack + ((size_t)rb * op.kc + kc0) * XQ4G_UNIT_BYTES, bytes, &full[slot]);
+                        if (xs) {
+                            if (!prep_done) {  // weights stream before this; the slices only after the prep
+                                xq4d::grid_dep_wait();
+                                prep_done = true;
+                            }
+                            xq4d::bulk_g2s(dst + kStageBytes, op.xh_img + (size_t)kc0 * XQ4G_KCHUNK, kChainXBytes,
+                                           &full[slot]);
+                            xq4d::bulk_g2s(dst + kStageBytes + kChainXBytes, op.xh_tbl1 + (size_t)kc0 * 2, kChainTBytes,
+                                           &full[slot]);
+                        }
                         if (++slot == kChainStages) {
                             slot = 0;
                             phase ^= 1;
@@ -1033,13 +1072,13 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
         for (int rb = rb0; rb < rb1; rb++, rbl++) {
             for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {
-                const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
+                const uint32_t stage = ring_s + (uint32_t)slot * kChainStageBytes;
                 const bool whole = kc0 + kStageChunks <= op.kc;
                 bool ok;
 #ifndef XQ4_CHAIN_NO_M1
-                if (op.xh && op.m == 1 && whole)  // one token, fp16 path, whole stage: the M1 form
-                    ok = consume_stage<1, false, true, false, true, true>(stage, &full[slot], phase, kc0, op.kc, op.k,
-                                                                         xr, xs, 0u, warp, lane, acc, op.xh_tbl);
+                if (op.xh && op.m == 1 && whole)  // one token, fp16 path, whole stage: x and table in the stage
+                    ok = consume_stage<1, false, true, false, true, true, true>(stage, &full[slot], phase, kc0, op.kc,
+                                                                               op.k, xr, xs, 0u, warp, lane, acc);
                 else
 #endif
                 if (op.xh)  // fp16 path: K padding is zero in the image

@@ -15,6 +15,7 @@ static __device__ unsigned int g_xq4_fault;
 #define XQ4_FAULT_GEMM_WAIT 0x4u
 #define XQ4_FAULT_PEER_WAIT 0x8u  // a peer GPU's output words did not arrive in time
 #define XQ4_FAULT_CHAIN_WAIT 0x10u  // a chain op's wait for the previous op ran out
+#define XQ4_FAULT_ATTN_POS 0x20u    // decode attention given a position outside its cache (nothing written)
 
 namespace xq4d {
 

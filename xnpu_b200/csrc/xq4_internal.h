@@ -68,6 +68,7 @@ struct xq4_chain_op_dev {
     int xh;               // x comes from a prepared fp16 image (below) instead of x
     const uint16_t *xh_img;    // [m][kc*64] fp16, x scaled by a per-token power of two
     const float4 *xh_tbl;      // [kc][4][2]: the zero-point MMA accumulator inputs per group
+    const float4 *xh_tbl1;     // m == 1: [kc][2] the same inputs of token 0, {z, z, 16 z, 16 z} per group
     const unsigned *xh_max;    // [8] per-token max |x| (bf16 magnitude bits)
     // Work split: a segment is a run of ops of which only the first waits
     // for its predecessor; its row blocks, weighted by ring stages, are cut
@@ -113,6 +114,7 @@ struct xq4_chain_prep_dev {
     const void *x;        // bf16 [m][k]
     uint16_t *img;
     float *tbl;
+    float4 *tbl1;         // m == 1: the one-token table (xq4_chain_op_dev::xh_tbl1)
     unsigned *max;
     int m, k, kc, norm;   // norm: RMS-normalise x with norm_w first
     const uint16_t *norm_w;
@@ -166,6 +168,7 @@ cudaError_t xq4_launch_w4a8(const uint8_t *pack, int n, int k, const void *qx, c
 unsigned int xq4_take_fault_gemv();
 unsigned int xq4_take_fault_gemm();
 unsigned int xq4_take_fault_w4a8();
+unsigned int xq4_take_fault_attn();
 cudaStream_t xq4_device_cuda_stream(struct xq4_device *dev);
 int xq4_device_ordinal(const struct xq4_device *dev);
 #endif

@@ -273,6 +273,42 @@ class Chain:
             pass
 
 
+class Attention:
+    """Decode attention of one token per layer (RoPE, per-head q/k RMSNorm,
+    KV-cache append, GQA attention) on the device: the reference's decode
+    glue (crates/xnpu-cli/src/main.rs:4817-4857, :4967-5033); see
+    xq4_attn_decode."""
+
+    def __init__(self, dev, heads, nkv, cache_seq, rope_base=10000.0):
+        h = ctypes.c_void_p()
+        check(lib().xq4_attn_create(dev.handle, heads, nkv, cache_seq, float(rope_base), ctypes.byref(h)))
+        self._h, self.dev = h, dev
+        self.heads, self.nkv, self.cache_seq = heads, nkv, cache_seq
+
+    def decode(self, qkv, k_cache, v_cache, pos, out=None, q_norm=None, k_norm=None, stream=None):
+        """qkv: CUDA bf16 [heads*128 + 2*nkv*128]; caches bf16 [nkv, cache_seq,
+        128]; pos: CUDA int32 tensor of one element.  Returns out bf16
+        [heads*128]."""
+        import torch
+        if out is None:
+            out = torch.empty(self.heads * 128, dtype=torch.bfloat16, device=qkv.device)
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        check(lib().xq4_attn_decode(self._h, qkv.data_ptr(), ptr(q_norm), ptr(k_norm), k_cache.data_ptr(),
+                                    v_cache.data_ptr(), pos.data_ptr(), out.data_ptr(), _torch_stream(stream)))
+        return out
+
+    def destroy(self):
+        if self._h:
+            lib().xq4_attn_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
 def timeline_wait(dev, seq, timeout_ns):
     """Wait until op ``seq`` (and all before it) completed; raise on timeout."""
     check(lib().xq4_wait(dev.handle, seq, int(timeout_ns)))
