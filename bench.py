@@ -412,6 +412,7 @@ def main():
                    "config2_gate_batch_sweep": config2_run(dev, stream, timed, peak),
                    "config3_prefill_gemm": config3_run(dev, stream, timed)}
     w4a8 = None if (args.skip_configs or world > 1) else w4a8_run(weights, xs, stream, timed, args)
+    dstep = None if args.skip_configs else decode_step_run(dev, weights, comm, world, stream, timed, args, peak)
 
     if rank == 0:
         cpu = None if args.no_cpu_baseline or world > 1 else cpu_baseline()
@@ -436,6 +437,7 @@ def main():
             "lm_head": lm,
             "configs": configs,
             "w4a8": w4a8,
+            "decode_step": dstep,
             "sharded_parity": sharded_parity,
             "device": meta["name"],
         }
@@ -675,6 +677,55 @@ def config3_run(dev, stream, timed, copies=3, reps=12):
     return {"shape": "m=2048, k=4096, n=14336", "flops": fl, "us": us,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": burst, "unit": "TFLOP/s", "frac": tf / burst,
                          "peak_kind": "measured burst (cuBLAS bf16)", "frac_of_sustained": tf / sustained}}
+
+
+def decode_step_run(dev, weights, comm, world, stream, timed, args, peak, pos=1024, cache_seq=4096):
+    """Config 4's full decode step: the 32 layers of the benchmark's weights
+    as a Llama-3-8B decoder (32 q heads over 8 kv heads, head dim 128, RoPE
+    base 500000, random-init RMSNorm weights), one token at context position
+    `pos` over 4096-position KV caches: per layer RMSNorm + qkv, RoPE +
+    KV-cache append + GQA attention, o + residual, RMSNorm + gate/up + SwiGLU
+    (column-sharded at N > 1) + down + residual (xnpu_b200.decode, 7 launches
+    per layer), captured once in a CUDA graph and replayed."""
+    import torch
+    from xnpu_b200 import decode, synth
+    rng = np.random.default_rng(4242)
+
+    def norm_w(n):
+        w = synth.f32_to_bf16_bits((1.0 + 0.02 * rng.standard_normal(n)).astype(np.float32))
+        return torch.from_numpy(w.view(np.int16)).cuda().view(torch.bfloat16)
+
+    layers = [decode.DecodeLayerWeights(lw["qkv"], lw["o"], lw["gateup"], lw["down"], norm_w(4096), norm_w(4096))
+              for lw in weights]
+    step = decode.DecodeStep(dev, layers, 4096, 32, 8, cache_seq, rope_base=500000.0, comm=comm, world=world)
+    for kc, vc in zip(step.k_cache, step.v_cache):  # earlier tokens' keys and values
+        kc.normal_()
+        vc.normal_()
+    step.x.normal_()
+    step.pos.fill_(pos)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step.run(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step.run(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+    ms = timed(lambda i: graph.replay(), args.steps)
+    finite = bool(torch.isfinite(step.x.float()).all().item())
+    del graph
+    step.destroy()
+    kv_bytes = LAYERS * 8 * (pos + 1) * 2 * 128 * 2
+    b = step_bytes_per_gpu(world) + kv_bytes
+    gbs = b / (ms * 1e-3) / 1e9
+    return {"tok_s": 1e3 / ms, "ms_per_step": ms, "context_pos": pos, "cache_seq": cache_seq,
+            "launches_per_step": step.launches_per_step, "output_finite": finite,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "bytes": b, "kv_cache_bytes": kv_bytes},
+            "path": "per layer: chain(RMSNorm + qkv) -> xq4_attn_decode -> chain(o + residual) -> "
+                    "chain(RMSNorm + gate/up + SwiGLU, down + residual); one CUDA graph per token"}
 
 
 def e2e_run(dev, weights, comm, world, args):
