@@ -234,6 +234,14 @@ typedef struct xq4_chain_op {
     float norm_eps;
     const void *residual_dev;
     int swiglu;
+    /* Non-zero: the op runs in the W4A8 parity mode of xq4_linear_w4a8 (the
+     * reference's NPU numerics): the chain's prep quantizes x -- after the
+     * RMSNorm, when norm_w_dev is given: the reference's fused rms -> quant
+     * -> GEMV pair, crates/xnpu-cli/src/main.rs:7802-7815 -- per 32-K group
+     * to int8 exactly as xq4_quantize_x (w4u_quantize_x, main.rs:2955-2986),
+     * and the op's output is the xq4_linear_w4a8 result for it, bit for bit.
+     * x must be an activation no op of the chain writes. */
+    int w4a8;
 } xq4_chain_op;
 int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_ops, xq4_chain **out);
 int xq4_chain_destroy(xq4_chain *chain);

@@ -71,7 +71,7 @@ class ChainOp(ctypes.Structure):
         ("m", ctypes.c_int), ("out_dtype", ctypes.c_int), ("wait_prev", ctypes.c_int),
         ("comm", ctypes.c_void_p),
         ("norm_w_dev", ctypes.c_void_p), ("norm_eps", ctypes.c_float), ("residual_dev", ctypes.c_void_p),
-        ("swiglu", ctypes.c_int),
+        ("swiglu", ctypes.c_int), ("w4a8", ctypes.c_int),
     ]
 
 

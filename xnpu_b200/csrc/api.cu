@@ -431,6 +431,9 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.xh_img = nullptr;
         d.xh_tbl = nullptr;
         d.xh_tbl1 = nullptr;
+        d.w4a8 = 0;
+        d.qx_img = nullptr;
+        d.qx_tbl = nullptr;
         d.xh_max = nullptr;
         d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
         d.shard = o.comm && p2p.nranks > 1;
@@ -480,7 +483,8 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         int m, k;
         const void *norm_w;
         float eps;
-        size_t img_off, tbl_off, tbl1_off, max_off;
+        int w4a8;
+        size_t img_off, tbl_off, tbl1_off, max_off, qx_off, qtbl_off;
     };
     // bytes of op j's output
     const auto y_bytes = [&](int j) {
@@ -505,22 +509,32 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         if (written) {
             if (o.norm_w_dev)
                 return xq4_fail(XQ4_EINVAL, "op %d: RMSNorm needs an activation no op of the chain writes", i);
+            if (o.w4a8)
+                return xq4_fail(XQ4_EINVAL, "op %d: W4A8 needs an activation no op of the chain writes", i);
             continue;
         }
+        const int w8 = o.w4a8 != 0;
         int pi = -1;
         for (size_t q = 0; q < preps.size(); q++)
-            if (preps[q].x == o.x_dev && preps[q].m == o.m && preps[q].k == o.w->k &&
+            if (preps[q].x == o.x_dev && preps[q].m == o.m && preps[q].k == o.w->k && preps[q].w4a8 == w8 &&
                 preps[q].norm_w == o.norm_w_dev && (!o.norm_w_dev || preps[q].eps == o.norm_eps))
                 pi = (int)q;
         if (pi < 0) {
-            prep_key pk{o.x_dev, o.m, o.w->k, o.norm_w_dev, o.norm_eps, 0, 0, 0, 0};
+            prep_key pk{o.x_dev, o.m, o.w->k, o.norm_w_dev, o.norm_eps, w8, 0, 0, 0, 0, 0, 0};
             const size_t kp = (size_t)o.w->kc * XQ4G_KCHUNK;
-            pk.img_off = img_bytes;
-            img_bytes += align((size_t)o.m * kp * 2);
-            pk.tbl_off = img_bytes;
-            img_bytes += align((size_t)o.w->kc * 32 * sizeof(float));
-            pk.tbl1_off = img_bytes;
-            img_bytes += align((size_t)o.w->kc * 2 * sizeof(float4));
+            if (w8) {  // int8 image and the per-group table
+                pk.qx_off = img_bytes;
+                img_bytes += align((size_t)o.m * kp);
+                pk.qtbl_off = img_bytes;
+                img_bytes += align((size_t)o.w->kc * 2 * 8 * sizeof(int2));
+            } else {  // fp16 image and its zero-point tables
+                pk.img_off = img_bytes;
+                img_bytes += align((size_t)o.m * kp * 2);
+                pk.tbl_off = img_bytes;
+                img_bytes += align((size_t)o.w->kc * 32 * sizeof(float));
+                pk.tbl1_off = img_bytes;
+                img_bytes += align((size_t)o.w->kc * 2 * sizeof(float4));
+            }
             pk.max_off = img_bytes;
             img_bytes += 256;
             pi = (int)preps.size();
@@ -560,15 +574,36 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     std::vector<xq4_chain_prep_dev> ptab(preps.size());
     for (size_t q = 0; q < preps.size(); q++) {
         const prep_key &pk = preps[q];
-        ptab[q] = xq4_chain_prep_dev{pk.x, (uint16_t *)(img + pk.img_off), (float *)(img + pk.tbl_off),
-                                     (float4 *)(img + pk.tbl1_off),
-                                     (unsigned *)(img + pk.max_off), pk.m, pk.k, (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK,
-                                     pk.norm_w != nullptr, (const uint16_t *)pk.norm_w, pk.eps, 0};
+        xq4_chain_prep_dev &pd = ptab[q];
+        pd = xq4_chain_prep_dev{};
+        pd.x = pk.x;
+        pd.max = (unsigned *)(img + pk.max_off);
+        pd.m = pk.m;
+        pd.k = pk.k;
+        pd.kc = (pk.k + XQ4G_KCHUNK - 1) / XQ4G_KCHUNK;
+        pd.norm = pk.norm_w != nullptr;
+        pd.norm_w = (const uint16_t *)pk.norm_w;
+        pd.eps = pk.eps;
+        pd.w4a8 = pk.w4a8;
+        if (pk.w4a8) {
+            pd.qx = (uint8_t *)(img + pk.qx_off);
+            pd.qtbl = (int2 *)(img + pk.qtbl_off);
+        } else {
+            pd.img = (uint16_t *)(img + pk.img_off);
+            pd.tbl = (float *)(img + pk.tbl_off);
+            pd.tbl1 = (float4 *)(img + pk.tbl1_off);
+        }
     }
     for (int i = 0; i < n_ops; i++) {
         const int pi = op_prep[(size_t)i];
         if (pi < 0) continue;
         xq4_chain_op_dev &d = tab[(size_t)i];
+        if (ptab[(size_t)pi].w4a8) {
+            d.w4a8 = 1;
+            d.qx_img = ptab[(size_t)pi].qx;
+            d.qx_tbl = ptab[(size_t)pi].qtbl;
+            continue;
+        }
         d.xh = 1;
         d.xh_img = ptab[(size_t)pi].img;
         d.xh_tbl = (const float4 *)ptab[(size_t)pi].tbl;

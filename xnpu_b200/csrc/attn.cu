@@ -46,10 +46,11 @@ namespace {
 constexpr int kHd = 128;          // head dim (fixed by the reference's model family)
 constexpr int kWarps = 4;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kTile = 32;         // positions per K/V tile
-constexpr int kKStride = kHd + 2; // K tile row stride (bf16): rows fall on distinct banks
+constexpr int kKStride = kHd + 2; // K row stride in shared memory (bf16): rows on distinct banks
 constexpr int kMaxGroup = 8;      // q heads per kv head
-constexpr int kMaxSpan = 2048;    // positions per CTA (scores kept in shared memory)
+constexpr int kMaxSpan = 384;     // positions per CTA (its K and V rows and scores in shared memory)
+constexpr int kMaxSplits = 64;    // splits per kv head (the merge covers them in two lane rounds)
+constexpr int kMinSpan = 128;     // positions a split takes before the token uses another split
 // One split's partial of one head in the workspace: max, sum, two pad words
 // (so that acc starts 16 bytes in), acc[128]; 528 bytes, a multiple of 16.
 constexpr int kRec = 4 + kHd;
@@ -64,7 +65,8 @@ struct attn_params {
     uint16_t *out;                    // [heads][128]
     float *ws;                        // [heads][splits][kRec]: max, sum, pad, acc
     unsigned *cnt;                    // [nkv] CTAs done (left zeroed)
-    int heads, nkv, cache_seq, splits, span;
+    int heads, nkv, cache_seq, splits;
+    int span;                         // positions the score area holds per head (a split's most)
 };
 
 // Floats of the score area, rounded up so that the tiles after it stay
@@ -114,6 +116,21 @@ __device__ void rope_norm_head(const uint16_t *src, const float *cs, const uint1
     __syncwarp();
 }
 
+// Asynchronous global -> shared copies (nothing held in registers while in
+// flight); completion by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(xq4d::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(xq4d::smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(kThreads)
 attn_decode_kernel(const attn_params p)
 {
@@ -121,15 +138,17 @@ attn_decode_kernel(const attn_params p)
     const int G = p.heads / p.nkv;
     float *qf = reinterpret_cast<float *>(smem);                                     // [G][128]
     float *sc = qf + kMaxGroup * kHd;                                                // [G][span]
-    uint16_t *kt = reinterpret_cast<uint16_t *>(sc + sc_floats(G, p.span));         // [kTile][kKStride]
-    uint16_t *vt = kt + kTile * kKStride;                                            // [kTile][128]
-    uint16_t *tmp = vt + kTile * kHd;                                                // [kWarps][128] bf16 scratch
-    __shared__ __align__(16) uint16_t knew[kHd];
-    __shared__ __align__(16) uint16_t vnew[kHd];
+    uint16_t *vt = reinterpret_cast<uint16_t *>(sc + sc_floats(G, p.span));         // [span][128]
+    uint16_t *kt = vt + (size_t)p.span * kHd;                                        // [span][kKStride]
+    uint16_t *tmp = kt + (size_t)p.span * kKStride;                                  // [kWarps][128] bf16 scratch
     __shared__ bool last;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int split = blockIdx.x, kv = blockIdx.y;
+    // the next kernel (the o projection's chain) may launch now and stream
+    // its weights while this one runs; it reads this kernel's output only
+    // after its own griddepcontrol.wait
+    xq4d::grid_dep_launch();
     xq4d::grid_dep_wait();  // qkv and the cache come from the preceding kernels
     const int pos = *p.pos;
     if (pos < 0 || pos >= p.cache_seq) {  // the host cannot check a device-resident position
@@ -137,95 +156,109 @@ attn_decode_kernel(const attn_params p)
         return;
     }
     const int s = pos + 1;
-    const int t0 = split * p.span, t1 = min(s, t0 + p.span);
+    // splits for this token: at least kMinSpan positions each (a split is
+    // latency-bound, and the merge reads every split), at most p.splits;
+    // never more positions than the span the shared memory was sized for
+    const int nsp = min(p.splits, max(1, (s + kMinSpan - 1) / kMinSpan));
+    const int span = (s + nsp - 1) / nsp;
+    const int t0 = split * span, t1 = min(s, t0 + span);
+    const int nt = max(0, t1 - t0);
     const float *cs = p.rope ? p.rope + (size_t)pos * kHd : nullptr;
 
-    // q heads of this group: RoPE + norm, kept in f32
+    // every K and V row of the span in flight at once (the token's own row,
+    // position pos, comes from this kernel instead); K rows land at a padded
+    // stride, so in 4-byte pieces
+    {
+        const size_t base = ((size_t)kv * p.cache_seq + t0) * kHd;
+        for (int i = threadIdx.x; i < nt * (kHd / 8); i += kThreads) {  // V: 16-byte pieces
+            const int r = i / (kHd / 8), c = i % (kHd / 8);
+            if (t0 + r != pos) cp_async16(vt + r * kHd + 8 * c, p.vc + base + (size_t)r * kHd + 8 * c);
+        }
+        for (int i = threadIdx.x; i < nt * (kHd / 2); i += kThreads) {  // K: 4-byte pieces
+            const int r = i / (kHd / 2), c = i % (kHd / 2);
+            if (t0 + r != pos) cp_async4(kt + r * kKStride + 2 * c, p.kc + base + (size_t)r * kHd + 2 * c);
+        }
+    }
+    // q heads of this group: RoPE + norm, kept in f32 (while the rows land)
     for (int hg = warp; hg < G; hg += kWarps)
         rope_norm_head(p.qkv + (size_t)(kv * G + hg) * kHd, cs, p.q_norm, tmp + warp * kHd, qf + hg * kHd, lane);
-    // the CTA holding position pos appends the token's k (RoPE + norm) and v
+    // the CTA holding position pos appends the token's k (RoPE + norm) and v,
+    // to the caches and straight into its rows of the span
     if (pos >= t0 && pos < t1 && warp == 0) {
-        rope_norm_head(p.qkv + (size_t)(p.heads + kv) * kHd, cs, p.k_norm, knew, nullptr, lane);
+        uint16_t *kr = kt + (pos - t0) * kKStride, *vr = vt + (pos - t0) * kHd;
+        rope_norm_head(p.qkv + (size_t)(p.heads + kv) * kHd, cs, p.k_norm, kr, nullptr, lane);
         const uint16_t *v = p.qkv + (size_t)(p.heads + p.nkv + kv) * kHd;
-        for (int j = lane; j < kHd; j += 32) vnew[j] = v[j];
+        for (int j = lane; j < kHd; j += 32) vr[j] = v[j];
         __syncwarp();
         const size_t row = ((size_t)kv * p.cache_seq + pos) * kHd;
         for (int j = lane; j < kHd; j += 32) {
-            p.kc[row + j] = knew[j];
-            p.vc[row + j] = vnew[j];
+            p.kc[row + j] = kr[j];
+            p.vc[row + j] = vr[j];
         }
     }
+    cp_async_wait_all();
     __syncthreads();
 
     const float rs = sqrtf(128.f);  // (128f32).sqrt(): exact to f32 rounding
     float mx[kMaxGroup / kWarps];
     for (int i = 0; i < kMaxGroup / kWarps; i++) mx[i] = -INFINITY;
-    // pass 1: scores of the span, tile by tile
-    for (int tb = t0; tb < t1; tb += kTile) {
-        const int nt = min(kTile, t1 - tb);
-        const size_t base = ((size_t)kv * p.cache_seq + tb) * kHd;
-        for (int i = threadIdx.x; i < nt * (kHd / 8); i += kThreads) {  // 16-byte pieces
-            const int r = i / (kHd / 8), c = i % (kHd / 8);
-            uint4 v = *reinterpret_cast<const uint4 *>(p.kc + base + (size_t)r * kHd + 8 * c);
-            if (tb + r == pos) v = *reinterpret_cast<const uint4 *>(knew + 8 * c);
-            uint32_t *d = reinterpret_cast<uint32_t *>(kt + r * kKStride + 8 * c);
-            d[0] = v.x;
-            d[1] = v.y;
-            d[2] = v.z;
-            d[3] = v.w;
-        }
-        __syncthreads();
-        for (int hg = warp, i = 0; hg < G; hg += kWarps, i++) {
-            float d = 0.f;
-            if (lane < nt) {  // d = sum_j k[t][j] * q[j], j ascending (main.rs:5006-5011)
-                const uint32_t *kr = reinterpret_cast<const uint32_t *>(kt + lane * kKStride);
-                const float *q = qf + hg * kHd;
-                for (int j2 = 0; j2 < kHd / 2; j2++) {
-                    const uint32_t w = kr[j2];
-                    d = __fadd_rn(d, __fmul_rn(__uint_as_float(w << 16), q[2 * j2]));
-                    d = __fadd_rn(d, __fmul_rn(__uint_as_float(w & 0xFFFF0000u), q[2 * j2 + 1]));
-                }
-                d = __fdiv_rn(d, rs);
-                sc[hg * p.span + (tb - t0) + lane] = d;
-            }
-            float m = lane < nt ? d : -INFINITY;
+    // pass 1: the scores; lane l takes positions l, l+32, ... of the span,
+    // four at a time (independent sums), each over j ascending
+    // (d = sum_j k[t][j] * q[j], main.rs:5006-5011)
+    for (int hg = warp, i = 0; hg < G; hg += kWarps, i++) {
+        const float *q = qf + hg * kHd;
+        float m = -INFINITY;
+        for (int tb = 0; tb < nt; tb += 128) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t *kr[4];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            mx[i] = fmaxf(mx[i], m);
+            for (int u = 0; u < 4; u++) {  // rows past the span read the last row; their sums are dropped
+                const int t = min(tb + lane + 32 * u, nt - 1);
+                kr[u] = reinterpret_cast<const uint32_t *>(kt + t * kKStride);
+            }
+            for (int j2 = 0; j2 < kHd / 2; j2++) {
+                const float q0 = q[2 * j2], q1 = q[2 * j2 + 1];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t w = kr[u][j2];
+                    d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w << 16), q0));
+                    d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w & 0xFFFF0000u), q1));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int t = tb + lane + 32 * u;
+                if (t < nt) {
+                    const float dv = __fdiv_rn(d[u], rs);
+                    sc[hg * span + t] = dv;
+                    m = fmaxf(m, dv);
+                }
+            }
         }
-        __syncthreads();
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        mx[i] = m;
     }
     // pass 2: weights w_t = exp(s_t - max), their sum, and sum_t w_t v_t
     // (each lane owns dims 4*lane..4*lane+3, t ascending)
     float acc[kMaxGroup / kWarps][4] = {};
     float sum[kMaxGroup / kWarps] = {};
     for (int hg = warp, i = 0; hg < G; hg += kWarps, i++)
-        for (int t = lane; t < t1 - t0; t += 32) {
-            float *e = sc + hg * p.span + t;
+        for (int t = lane; t < nt; t += 32) {
+            float *e = sc + hg * span + t;
             *e = expf(__fsub_rn(*e, mx[i]));
             sum[i] = __fadd_rn(sum[i], *e);
         }
-    for (int tb = t0; tb < t1; tb += kTile) {
-        const int nt = min(kTile, t1 - tb);
-        const size_t base = ((size_t)kv * p.cache_seq + tb) * kHd;
-        __syncthreads();  // the previous tile is consumed (and pass 1's weights written)
-        for (int i = threadIdx.x; i < nt * (kHd / 8); i += kThreads) {
-            const int r = i / (kHd / 8), c = i % (kHd / 8);
-            uint4 v = *reinterpret_cast<const uint4 *>(p.vc + base + (size_t)r * kHd + 8 * c);
-            if (tb + r == pos) v = *reinterpret_cast<const uint4 *>(vnew + 8 * c);
-            *reinterpret_cast<uint4 *>(vt + r * kHd + 8 * c) = v;
+    __syncwarp();
+    for (int hg = warp, i = 0; hg < G; hg += kWarps, i++)
+        for (int r = 0; r < nt; r++) {
+            const float w = sc[hg * span + r];
+            const uint2 v = *reinterpret_cast<const uint2 *>(vt + r * kHd + 4 * lane);
+            acc[i][0] = __fadd_rn(acc[i][0], __fmul_rn(w, __uint_as_float(v.x << 16)));
+            acc[i][1] = __fadd_rn(acc[i][1], __fmul_rn(w, __uint_as_float(v.x & 0xFFFF0000u)));
+            acc[i][2] = __fadd_rn(acc[i][2], __fmul_rn(w, __uint_as_float(v.y << 16)));
+            acc[i][3] = __fadd_rn(acc[i][3], __fmul_rn(w, __uint_as_float(v.y & 0xFFFF0000u)));
         }
-        __syncthreads();
-        for (int hg = warp, i = 0; hg < G; hg += kWarps, i++)
-            for (int r = 0; r < nt; r++) {
-                const float w = sc[hg * p.span + (tb - t0) + r];
-                const uint2 v = *reinterpret_cast<const uint2 *>(vt + r * kHd + 4 * lane);
-                acc[i][0] = __fadd_rn(acc[i][0], __fmul_rn(w, __uint_as_float(v.x << 16)));
-                acc[i][1] = __fadd_rn(acc[i][1], __fmul_rn(w, __uint_as_float(v.x & 0xFFFF0000u)));
-                acc[i][2] = __fadd_rn(acc[i][2], __fmul_rn(w, __uint_as_float(v.y << 16)));
-                acc[i][3] = __fadd_rn(acc[i][3], __fmul_rn(w, __uint_as_float(v.y & 0xFFFF0000u)));
-            }
-    }
     // this split's (max, sum, acc) per head
     for (int hg = warp, i = 0; hg < G; hg += kWarps, i++) {
         float sm = sum[i];
@@ -245,22 +278,38 @@ attn_decode_kernel(const attn_params p)
     __syncthreads();
     if (!last) return;
     __threadfence();
+    // splits that hold positions (the rest are empty for this token)
+    const int used = (s + span - 1) / span;
     for (int hg = warp; hg < G; hg += kWarps) {
         const float *w = p.ws + (size_t)(kv * G + hg) * p.splits * kRec;
-        float M = -INFINITY;
-        for (int sp = 0; sp < p.splits; sp++) M = fmaxf(M, __ldcg(w + (size_t)sp * kRec));
-        float L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int sp = 0; sp < p.splits; sp++) {
-            const float *ws = w + (size_t)sp * kRec;
-            const float l = __ldcg(ws + 1);
-            if (l == 0.f) continue;  // an empty split
-            const float f = p.splits == 1 ? 1.f : expf(__fsub_rn(__ldcg(ws), M));
-            L = __fadd_rn(L, __fmul_rn(l, f));
-            const float4 a = __ldcg(reinterpret_cast<const float4 *>(ws + kRecAcc + 4 * lane));
-            o[0] = __fadd_rn(o[0], __fmul_rn(a.x, f));
-            o[1] = __fadd_rn(o[1], __fmul_rn(a.y, f));
-            o[2] = __fadd_rn(o[2], __fmul_rn(a.z, f));
-            o[3] = __fadd_rn(o[3], __fmul_rn(a.w, f));
+        // lane-parallel over the splits: the maximum, each split's factor
+        // exp(m_s - M), and the weighted sum of the split sums
+        float ms[2], ls[2], M = -INFINITY;
+        for (int r = 0; r < 2; r++) {
+            const int sp = lane + 32 * r;
+            ms[r] = sp < used ? __ldcg(w + (size_t)sp * kRec) : -INFINITY;
+            ls[r] = sp < used ? __ldcg(w + (size_t)sp * kRec + 1) : 0.f;
+            M = fmaxf(M, ms[r]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float f[2], L = 0.f;
+        for (int r = 0; r < 2; r++) {
+            f[r] = ls[r] == 0.f ? 0.f : (used == 1 ? 1.f : expf(__fsub_rn(ms[r], M)));
+            L = __fadd_rn(L, __fmul_rn(ls[r], f[r]));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L = __fadd_rn(L, __shfl_xor_sync(0xffffffffu, L, o));
+        // sum_s f_s acc_s: every lane's 4 dims, the splits' loads in flight together
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int sp = 0; sp < used; sp++) {
+            const float fs = __shfl_sync(0xffffffffu, f[sp >> 5], sp & 31);
+            const float4 a = __ldcg(reinterpret_cast<const float4 *>(w + (size_t)sp * kRec + kRecAcc + 4 * lane));
+            o[0] = __fadd_rn(o[0], __fmul_rn(a.x, fs));
+            o[1] = __fadd_rn(o[1], __fmul_rn(a.y, fs));
+            o[2] = __fadd_rn(o[2], __fmul_rn(a.z, fs));
+            o[3] = __fadd_rn(o[3], __fmul_rn(a.w, fs));
         }
         uint16_t *out = p.out + (size_t)(kv * G + hg) * kHd + 4 * lane;
         for (int c = 0; c < 4; c++) out[c] = to_bf(__fdiv_rn(o[c], L));
@@ -308,15 +357,22 @@ extern "C" int xq4_attn_create(xq4_device *dev, int heads, int nkv, int cache_se
     // at most kMaxSpan positions and at least one tile
     int splits = (2 * sms + nkv - 1) / nkv;
     splits = std::max(splits, (cache_seq + kMaxSpan - 1) / kMaxSpan);
-    splits = std::min(splits, (cache_seq + kTile - 1) / kTile);
+    splits = std::min(splits, (cache_seq + 31) / 32);
+    splits = std::min(splits, kMaxSplits);
     const int span = (cache_seq + splits - 1) / splits;
+    if (span > kMaxSpan)
+        return xq4_fail(XQ4_EINVAL, "cache_seq %d needs more than %d splits of at most %d positions", cache_seq,
+                        kMaxSplits, kMaxSpan);
     splits = (cache_seq + span - 1) / span;
     const int G = heads / nkv;
-    xq4_attn *a = new (std::nothrow) xq4_attn{dev, ordinal, heads, nkv, cache_seq, splits, span, nullptr, nullptr,
-                                              nullptr, 0};
+    // the score area holds a split's positions: at most `span` when every
+    // split is in use, fewer than kMinSpan otherwise (see the kernel)
+    const int span_max = std::max(span, kMinSpan);
+    xq4_attn *a = new (std::nothrow) xq4_attn{dev, ordinal, heads, nkv, cache_seq, splits, span_max, nullptr,
+                                              nullptr, nullptr, 0};
     if (!a) return xq4_fail(XQ4_ENOMEM, "host allocation");
-    a->smem = sizeof(float) * ((size_t)kMaxGroup * kHd + sc_floats(G, span)) +
-              sizeof(uint16_t) * ((size_t)kTile * kKStride + (size_t)kTile * kHd + (size_t)kWarps * kHd);
+    a->smem = sizeof(float) * ((size_t)kMaxGroup * kHd + sc_floats(G, span_max)) +
+              sizeof(uint16_t) * ((size_t)span_max * kKStride + (size_t)span_max * kHd + (size_t)kWarps * kHd);
     const size_t ws_bytes = sizeof(float) * (size_t)heads * splits * kRec;
     if (rope_base > 0.f) {
         // the reference's rope_table (main.rs:4817-4827) at every position, in

@@ -712,9 +712,13 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     __shared__ unsigned smax[8];
     __shared__ float sinv[8];
     if (threadIdx.x < 8) smax[threadIdx.x] = 0u;
-    for (int i = threadIdx.x; i < p.kc * 32; i += kPrepThreads) p.tbl[i] = 0.f;
-    if (p.m == 1)  // a half chunk's missing group keeps a zero entry
-        for (int i = threadIdx.x; i < p.kc * 2; i += kPrepThreads) p.tbl1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.w4a8) {  // groups past K and tokens past m keep zero entries
+        for (int i = threadIdx.x; i < p.kc * 2 * 8; i += kPrepThreads) p.qtbl[i] = make_int2(0, 0);
+    } else {
+        for (int i = threadIdx.x; i < p.kc * 32; i += kPrepThreads) p.tbl[i] = 0.f;
+        if (p.m == 1)  // a half chunk's missing group keeps a zero entry
+            for (int i = threadIdx.x; i < p.kc * 2; i += kPrepThreads) p.tbl1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (p.norm) {
         // RMSNorm (crates/xnpu-cli/src/main.rs:4714-4724): warp w sums the
         // squares of token w, lane-strided then a fixed butterfly, so the
@@ -765,6 +769,59 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     }
     __syncthreads();
     const int lane = threadIdx.x & 31;
+    if (p.w4a8) {
+        // W4A8: per 32-K group (four consecutive runs, four neighbouring
+        // lanes) the reference's quantizer (w4u_quantize_x, main.rs:2955-2986):
+        // d = RNE_bf16(max|x| / 127), q = clamp(rne(x / d), -127, 127); an
+        // all-zero group gives q = 0 and d = 0.  q is stored with its bytes
+        // in the integer MMA's slot order (0, 2, 1, 3 within each 4), the
+        // table entry is {-8 * sum(q), f32 bits of d} per (group, token).
+        for (int base = 0; base < total_runs; base += kPrepThreads) {  // uniform trip count: shuffles below
+            const int r = base + threadIdx.x;
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            int tok = 0, kk = 0;
+            if (r < total_runs) {
+                tok = r / runs;
+                kk = 8 * (r - tok * runs);
+                uint32_t w[4];
+                run_words(r, tok, kk, w);
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    v[2 * h] = __uint_as_float(w[h] << 16);
+                    v[2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
+                }
+            }
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            uint32_t qb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            int qs = 0;
+            float df = 0.f;
+            if (amax != 0.f) {
+                df = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(amax, 127.f)));
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int q = (int)fminf(fmaxf(rintf(__fdiv_rn(v[i], df)), -127.f), 127.f);
+                    qs += q;
+                    qb[i] = (uint32_t)q & 0xFFu;
+                }
+            }
+            qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+            qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+            if (r < total_runs) {
+                const uint32_t w0 = qb[0] | (qb[2] << 8) | (qb[1] << 16) | (qb[3] << 24);
+                const uint32_t w1 = qb[4] | (qb[6] << 8) | (qb[5] << 16) | (qb[7] << 24);
+                *reinterpret_cast<uint2 *>(p.qx + (size_t)tok * kp + kk) = make_uint2(w0, w1);
+                if ((lane & 3) == 0) p.qtbl[(size_t)(kk >> 5) * 8 + tok] = make_int2(-8 * qs, __float_as_int(df));
+            }
+        }
+        const int pad_runs = (kp - p.k) / 8;
+        for (int i = threadIdx.x; i < p.m * pad_runs; i += kPrepThreads)
+            *reinterpret_cast<uint2 *>(p.qx + (size_t)(i / pad_runs) * kp + p.k + 8 * (i % pad_runs)) = make_uint2(0, 0);
+        return;
+    }
     for (int base = 0; base < total_runs; base += kPrepThreads) {  // uniform trip count: shuffles below
         const int r = base + threadIdx.x;
         float part = 0.f;
@@ -804,6 +861,49 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
     for (int i = threadIdx.x; i < p.m * pad_runs; i += kPrepThreads)
         *reinterpret_cast<uint4 *>(p.img + (size_t)(i / pad_runs) * kp + p.k + 8 * (i % pad_runs)) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x < 8) p.max[threadIdx.x] = smax[threadIdx.x];
+}
+
+// A chain stage of a W4A8 op: the integer tensor-core path of w4a8_kernel
+// (gemv_w4a8.cu), operation for operation, with the activation from the
+// prep's int8 image: per 32-K group one mma.m16n8k32 u8 x s8 of the raw
+// codes against q_x, accumulator input -8 * sum(q_x), then
+// acc += (s_w * d_x) * T in f32.
+__device__ __forceinline__ bool consume_stage_w4a8(uint32_t stage, uint64_t *full, uint32_t phase, int kc0, int kc_n,
+                                                   const uint8_t *xrow, const int2 *qtbl, int warp, int lane,
+                                                   float (&acc)[4])
+{
+    const int g = lane >> 2, t = lane & 3;
+    if (!xq4d::mbar_wait(full, phase)) return false;
+#pragma unroll
+    for (int c = 0; c < kCpw; c++) {
+        const int cl = warp + c * kConsumerWarps;  // chunk within the stage
+        const int kc = kc0 + cl;
+        if (kc < kc_n) {
+            const uint32_t up = stage + cl * XQ4G_UNIT_BYTES;
+            const uint4 cw = xq4d::lds_v4(up + lane * 16);
+            const uint2 sw = xq4d::lds_v2(up + XQ4G_CODE_BYTES + g * 8);
+            const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+            for (int G2 = 0; G2 < 2; G2++) {
+                const int grp = kc * 2 + G2;
+                const uint2 b = xq4d::ldg_v2(xrow + grp * 32 + 8 * t);
+                const uint4 e = xq4d::ldg_v4(qtbl + grp * 8 + 2 * t);  // {cx(2t), d(2t), cx(2t+1), d(2t+1)}
+                const uint32_t w0 = words[2 * G2], w1 = words[2 * G2 + 1];
+                const uint32_t a[4] = {w0 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu,
+                                       (w1 >> 4) & 0x0F0F0F0Fu};
+                int T[4];
+                xq4d::mma_u8s8_16832(T, a, b.x, b.y, (int)e.x, (int)e.z);
+                const uint32_t sg = G2 ? sw.y : sw.x;
+                const float s_lo = __uint_as_float(sg << 16), s_hi = __uint_as_float(sg & 0xFFFF0000u);
+                const float d0 = __uint_as_float(e.y), d1 = __uint_as_float(e.w);
+                acc[0] = fmaf(s_lo * d0, (float)T[0], acc[0]);
+                acc[1] = fmaf(s_lo * d1, (float)T[1], acc[1]);
+                acc[2] = fmaf(s_hi * d0, (float)T[2], acc[2]);
+                acc[3] = fmaf(s_hi * d1, (float)T[3], acc[3]);
+            }
+        }
+    }
+    return true;
 }
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
@@ -900,29 +1000,56 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
             // writes one value per row pair)
             const size_t ystride = (size_t)(op.shard ? op.n_total : op.n) >> (op.swiglu ? 1 : 0);
             const int yoff = op.shard ? (op.row_off >> (op.swiglu ? 1 : 0)) : 0;
-            for (int rb = rb0; alive && rb < rb1; rb++, rbl++) {
-                const int buf = rbl % kRedBufs;
-                const uint32_t use = (uint32_t)(rbl / kRedBufs);
-                if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
-                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
-                    alive = false;  // still counted below, so no other CTA waits on this one
-                    break;
+            for (int rb = rb0; alive && rb < rb1; rb++) {
+                // the row block's outputs o = base + lane (o = tok * 16 + row
+                // in the block), j = base / 32: the sum of the 8 consumer
+                // warps' partials in warp order; for a W4A8 op, over the row
+                // block's stages (2048-K chunks), each chunk's sum rounded to
+                // bf16 and the partials added in f32 in chunk order, as
+                // w4a8_kernel (the reference's w4u_read_c, main.rs:3066-3091)
+                float val[4] = {0.f, 0.f, 0.f, 0.f};
+                const int nst = op.w4a8 ? op.spr : 1;
+                for (int st = 0; st < nst; st++, rbl++) {
+                    const int buf = rbl % kRedBufs;
+                    const uint32_t use = (uint32_t)(rbl / kRedBufs);
+                    if (!xq4d::mbar_wait(&red_full[buf], use & 1)) {
+                        atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                        alive = false;  // still counted below, so no other CTA waits on this one
+                        break;
+                    }
+                    const float *rd = red + (size_t)buf * kConsumerWarps * 128;  // [warp][tok][row]
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int oo = 32 * j + lane;
+                        if (oo < op.m * 16) {
+                            float sum = 0.f;
+#pragma unroll
+                            for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
+                            if (op.w4a8) {
+                                const float part = __bfloat162float(__float2bfloat16_rn(sum));
+                                val[j] = st == 0 ? part : val[j] + part;
+                            } else {
+                                val[j] = sum;
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
                 }
-                const float *rd = red + (size_t)buf * kConsumerWarps * 128;  // [warp][tok][row]
-                for (int base = 0; base < op.m * 16; base += 32) {  // uniform trip count: SwiGLU pairs lanes
+                if (!alive) break;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {  // uniform trip count: SwiGLU pairs lanes
+                    const int base = 32 * j;
+                    if (base >= op.m * 16) break;
                     const int oo = base + lane;
                     const int tok = oo >> 4, r = oo & 15;
                     const int row = rb * XQ4G_ROWS + r;
                     const bool valid = oo < op.m * 16 && row < op.n;
-                    float sum = 0.f;
-                    if (valid) {
-#pragma unroll
-                        for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
-                        if (op.xh) {  // undo 2^-24 and the token's power of two (exact)
-                            float f1, f2;
-                            pow2_split(24 - tok_exponent(op.xh_max[tok]), f1, f2);
-                            sum = sum * f1 * f2;
-                        }
+                    float sum = val[j];
+                    if (valid && op.xh) {  // undo 2^-24 and the token's power of two (exact)
+                        float f1, f2;
+                        pow2_split(24 - tok_exponent(op.xh_max[tok]), f1, f2);
+                        sum = sum * f1 * f2;
                     }
                     if (op.swiglu) {
                         // rows 2i (gate) and 2i+1 (up) sit in neighbouring
@@ -970,8 +1097,6 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                         }
                     }
                 }
-                __syncwarp();
-                if (lane == 0) xq4d::mbar_arrive(&red_free[buf]);
             }
             // Before an op that waits for this one (or at the end), the
             // peers' rows of this CTA's ranges of the pending sharded ops go
@@ -1067,14 +1192,37 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
         const int tok = g < op.m ? g : 0;
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
                                              : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
+        const uint8_t *const qrow = op.w4a8 ? op.qx_img + (size_t)tok * op.kc * XQ4G_KCHUNK : nullptr;
         int rb0, rb1;
         chain_range(rng, o, cta, G, rb0, rb1);
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
-        for (int rb = rb0; rb < rb1; rb++, rbl++) {
+        const float hs = op.xh ? 0.0625f : 1.f;  // fp16 path: rows g+8 summed 16 * c
+        // the warp's partials to buffer rbl % kRedBufs: per row block, or per
+        // stage (one 2048-K chunk partial) for a W4A8 op
+        const auto handoff = [&]() -> bool {
+            const int buf = rbl % kRedBufs;
+            const uint32_t use = (uint32_t)(rbl / kRedBufs);
+            if (use > 0 && !xq4d::mbar_wait(&red_free[buf], (use - 1) & 1)) return false;
+            float *r = red + (size_t)buf * kConsumerWarps * 128 + (size_t)warp * 128;
+            r[(2 * t) * 16 + g] = acc[0][0];
+            r[(2 * t + 1) * 16 + g] = acc[0][1];
+            r[(2 * t) * 16 + g + 8] = acc[0][2] * hs;
+            r[(2 * t + 1) * 16 + g + 8] = acc[0][3] * hs;
+            acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);
+            rbl++;
+            return true;
+        };
+        for (int rb = rb0; rb < rb1; rb++) {
             for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks) {
                 const uint32_t stage = ring_s + (uint32_t)slot * kChainStageBytes;
                 const bool whole = kc0 + kStageChunks <= op.kc;
                 bool ok;
+                if (op.w4a8)
+                    ok = consume_stage_w4a8(stage, &full[slot], phase, kc0, op.kc, qrow, op.qx_tbl, warp, lane,
+                                            acc[0]);
+                else
 #ifndef XQ4_CHAIN_NO_M1
                 if (op.xh && op.m == 1 && whole)  // one token, fp16 path, whole stage: x and table in the stage
                     ok = consume_stage<1, false, true, false, true, true, true>(stage, &full[slot], phase, kc0, op.kc,
@@ -1102,23 +1250,15 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                     slot = 0;
                     phase ^= 1;
                 }
+                if (op.w4a8 && !handoff()) {
+                    atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
+                    return;
+                }
             }
-            // row block complete: the warp's partials to buffer rbl % kRedBufs
-            const int buf = rbl % kRedBufs;
-            const uint32_t use = (uint32_t)(rbl / kRedBufs);
-            if (use > 0 && !xq4d::mbar_wait(&red_free[buf], (use - 1) & 1)) {
+            if (!op.w4a8 && !handoff()) {  // row block complete
                 atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
                 return;
             }
-            float *r = red + (size_t)buf * kConsumerWarps * 128 + (size_t)warp * 128;
-            const float hs = op.xh ? 0.0625f : 1.f;  // fp16 path: rows g+8 summed 16 * c
-            r[(2 * t) * 16 + g] = acc[0][0];
-            r[(2 * t + 1) * 16 + g] = acc[0][1];
-            r[(2 * t) * 16 + g + 8] = acc[0][2] * hs;
-            r[(2 * t + 1) * 16 + g + 8] = acc[0][3] * hs;
-            acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.f;
-            __syncwarp();
-            if (lane == 0) xq4d::mbar_arrive(&red_full[buf]);
         }
     }
 }

@@ -71,17 +71,6 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float f)
 }
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
 
-// D = A(16x32 u8, row) * B(32x8 s8, col) + C, s32.
-__device__ __forceinline__ void mma_u8s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                               int c0, int c1)
-{
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %10, %11};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
-}
-
 // One warp per (token, 32-K group): the reference's per-group quantizer.
 __global__ void quantize_kernel(const uint16_t *__restrict__ x, int m, int k, int8_t *__restrict__ q,
                                 uint16_t *__restrict__ d)
@@ -279,7 +268,7 @@ w4a8_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n, co
                     const uint32_t a[4] = {w0 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu,
                                            (w1 >> 4) & 0x0F0F0F0Fu};
                     int T[4];
-                    mma_u8s8_16832(T, a, b.x, b.y, (int)cxp.x, (int)cxp.y);
+                    xq4d::mma_u8s8_16832(T, a, b.x, b.y, (int)cxp.x, (int)cxp.y);
                     const uint32_t sg = G2 ? sw.y : sw.x;
                     const float s_lo = __uint_as_float(sg << 16), s_hi = __uint_as_float(sg & 0xFFFF0000u);
                     const float d0 = __uint_as_float(ddp.x), d1 = __uint_as_float(ddp.y);

@@ -87,6 +87,12 @@ struct xq4_chain_op_dev {
     const uint16_t *residual;
     int swiglu;
     int wait_parity;      // phase parity of the consumers' op barrier at this op (waiting ops before it, mod 2)
+    // W4A8 (the reference's NPU numerics): x quantized by the prep to int8
+    // per 32-K group; per group one integer MMA, times s_w * d_x; each stage
+    // (2048 K) is one chunk partial, rounded to bf16 and summed in f32.
+    int w4a8;
+    const uint8_t *qx_img;     // [m][kc*64] int8, bytes 0,2,1,3 within each 4 (the MMA's slot order)
+    const int2 *qx_tbl;        // [groups][8 tokens]: {-8 * sum(q_x), bits of f32(d_x)}
 };
 
 // The chain's communicator side (nranks == 1: no sharded op).
@@ -119,7 +125,9 @@ struct xq4_chain_prep_dev {
     int m, k, kc, norm;   // norm: RMS-normalise x with norm_w first
     const uint16_t *norm_w;
     float eps;
-    int pad;
+    int w4a8;             // quantize to int8 (qx, qtbl) instead of the fp16 image
+    uint8_t *qx;          // [m][kc*64] (xq4_chain_op_dev::qx_img)
+    int2 *qtbl;           // [kc*2][8] (xq4_chain_op_dev::qx_tbl)
 };
 
 // A weight resident in HBM, in XQ4G layout.

@@ -228,7 +228,7 @@ class Chain:
     comm][, glue]) with raw device pointers (ints), an optional
     communicator handle for a column-sharded op and an optional dict of
     fused decode-step glue: {"norm_w": ptr, "eps": float, "residual": ptr,
-    "swiglu": bool}; see xq4_chain_create."""
+    "swiglu": bool, "w4a8": bool}; see xq4_chain_create."""
 
     def __init__(self, dev, ops):
         arr = (_lib.ChainOp * len(ops))()
@@ -239,7 +239,7 @@ class Chain:
             comm = op[6] if len(op) > 6 else None
             arr[i] = _lib.ChainOp(w.handle, xp, yp, m, od, 1 if wp else 0, getattr(comm, "value", comm),
                                   glue.get("norm_w"), float(glue.get("eps", 1e-5)), glue.get("residual"),
-                                  1 if glue.get("swiglu") else 0)
+                                  1 if glue.get("swiglu") else 0, 1 if glue.get("w4a8") else 0)
         h = ctypes.c_void_p()
         check(lib().xq4_chain_create(dev.handle, arr, len(ops), ctypes.byref(h)))
         self._h, self.dev, self.n_ops = h, dev, len(ops)
