@@ -10,8 +10,9 @@ reference's M9/P18 pairs (crates/xnpu-cli/src/main.rs:7802-7815).
     a chunk, ragged rows, 1 to 8 tokens, bf16 and f32 outputs, next to fp16
     ops and an op that waits for a W4A8 op's output).
   * With the RMSNorm fused in front (the prep normalises, then quantizes):
-    the prep sums the squares in its own fixed order (lane-strided f32 sums,
-    then a butterfly), which this test restates exactly on the CPU; from that
+    the prep sums the squares in its own fixed order (per-thread sums over
+    runs of 8, a butterfly per warp, the warps in order), which this test
+    restates exactly on the CPU; from that
     normalised activation the oracle quantizes (w4u_quantize_x) and runs its
     W4A8 GEMV, and the chain's output must meet the bound of
     test_gpu_w4a8.py (one bf16 ulp of each 2048-K chunk partial, at least
@@ -82,23 +83,31 @@ def test_w4a8_chain_ops_match_the_single_op(dev):
 
 
 def prep_rms_norm(x_bits, w_bits, eps=1e-5):
-    """The chain prep's RMSNorm, operation for operation in f32: lane l of
-    the token's warp sums x[i]^2 over i = l mod 32 in ascending i, a
-    butterfly (xor 16, 8, 4, 2, 1) adds the 32 sums, inv = 1 / sqrt(ss / k +
-    eps), out = RNE_bf16((x * inv) * w)."""
+    """The chain prep's RMSNorm, operation for operation in f32: thread i of
+    256 sums the squares of its runs of 8 activations (runs i, i + 256, ...,
+    each run's values in order), a butterfly (xor 16, 8, 4, 2, 1) adds each
+    warp's 32 sums, the 8 warp sums are added in warp order; inv = 1 /
+    sqrt(ss / k + eps), out = RNE_bf16((x * inv) * w)."""
     x = synth.bf16_bits_to_f32(x_bits).astype(np.float32)
     w = synth.bf16_bits_to_f32(w_bits).astype(np.float32)
     m, k = x.shape
     out = np.empty_like(x_bits)
     f32 = np.float32
+    runs = k // 8
     for t in range(m):
-        ss = np.zeros(32, dtype=np.float32)
-        for i in range(0, k, 32):
-            xb = x[t, i:i + 32]
-            ss = (ss + (xb * xb).astype(np.float32)).astype(np.float32)
+        ss = np.zeros(256, dtype=np.float32)
+        for r0 in range(0, runs, 256):
+            idx = np.arange(r0, min(runs, r0 + 256))
+            for e in range(8):
+                v = x[t, 8 * idx + e]
+                ss[idx - r0] = (ss[idx - r0] + (v * v).astype(np.float32)).astype(np.float32)
+        ws = ss.reshape(8, 32)
         for o in (16, 8, 4, 2, 1):
-            ss = (ss + ss[np.arange(32) ^ o]).astype(np.float32)
-        inv = f32(1.0) / np.sqrt(f32(f32(ss[0]) / f32(k)) + f32(eps))
+            ws = (ws + ws[:, np.arange(32) ^ o]).astype(np.float32)
+        tot = f32(0.0)
+        for i in range(8):
+            tot = f32(tot + ws[i, 0])
+        inv = f32(1.0) / np.sqrt(f32(f32(tot) / f32(k)) + f32(eps))
         out[t] = synth.f32_to_bf16_bits(((x[t] * inv).astype(np.float32) * w).astype(np.float32))
     return out
 

@@ -374,6 +374,7 @@ struct xq4_chain {
     xq4_chain_prep_dev *d_preps;
     const int2 *d_rng;        // [op][cta] row-block ranges
     int grid;                 // CTAs per launch (the range table's)
+    bool has_w4a8;            // some op runs in the W4A8 mode
     xq4_chain_p2p p2p;        // sharded ops' communicator (nranks 1: none)
     xq4_comm *comm;           // that communicator, or NULL
 };
@@ -621,10 +622,13 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         cudaFree(mem);
         return cuda_fail(e, "chain upload");
     }
+    bool has_w4a8 = false;
+    for (const xq4_chain_op_dev &d : tab) has_w4a8 = has_w4a8 || d.w4a8;
     xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
                                                 (unsigned *)(base + tab_bytes),
                                                 (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes),
-                                                (const int2 *)rng_d, grid, p2p, p2p.nranks > 1 ? comm : nullptr};
+                                                (const int2 *)rng_d, grid, has_w4a8, p2p,
+                                                p2p.nranks > 1 ? comm : nullptr};
     if (!c) {
         cudaFree(mem);
         return xq4_fail(XQ4_ENOMEM, "host allocation");
@@ -653,7 +657,7 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
     CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
-                             chain->n_preps, chain->p2p, (cudaStream_t)stream),
+                             chain->n_preps, chain->p2p, chain->has_w4a8, (cudaStream_t)stream),
        "chain launch");
     return XQ4_OK;
 }
@@ -667,7 +671,7 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
-                             chain->n_preps, chain->p2p, dev->stream),
+                             chain->n_preps, chain->p2p, chain->has_w4a8, dev->stream),
        "chain launch");
     const uint64_t s = dev->last_seq + 1;
     CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");

@@ -50,7 +50,7 @@ constexpr int kKStride = kHd + 2; // K row stride in shared memory (bf16): rows 
 constexpr int kMaxGroup = 8;      // q heads per kv head
 constexpr int kMaxSpan = 384;     // positions per CTA (its K and V rows and scores in shared memory)
 constexpr int kMaxSplits = 64;    // splits per kv head (the merge covers them in two lane rounds)
-constexpr int kMinSpan = 128;     // positions a split takes before the token uses another split
+constexpr int kMinSpan = 64;      // positions a split takes before the token uses another split (measured)
 // One split's partial of one head in the workspace: max, sum, two pad words
 // (so that acc starts 16 bytes in), acc[128]; 528 bytes, a multiple of 16.
 constexpr int kRec = 4 + kHd;

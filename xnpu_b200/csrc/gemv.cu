@@ -720,19 +720,37 @@ chain_prep_kernel(const xq4_chain_prep_dev *__restrict__ preps)
             for (int i = threadIdx.x; i < p.kc * 2; i += kPrepThreads) p.tbl1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (p.norm) {
-        // RMSNorm (crates/xnpu-cli/src/main.rs:4714-4724): warp w sums the
-        // squares of token w, lane-strided then a fixed butterfly, so the
-        // result is the same on every run; inv = 1 / sqrt(mean + eps)
+        // RMSNorm (crates/xnpu-cli/src/main.rs:4714-4724), inv = 1 / sqrt(mean
+        // of squares + eps), with the sum of squares in a fixed order, so the
+        // result is the same on every run: thread i sums its runs i, i + 256,
+        // ... (each run's 8 values in order), a butterfly adds a warp's 32
+        // sums, thread 0 adds the 8 warps' sums in warp order.  Every thread
+        // has its runs' loads in flight together.
+        __shared__ float wsum[kPrepThreads / 32];
         const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        if (w < p.m) {
+        for (int tk = 0; tk < p.m; tk++) {
             float ss = 0.f;
-            for (int i = lane; i < p.k; i += 32) {
-                const float v = __uint_as_float((uint32_t)x[(size_t)w * p.k + i] << 16);
-                ss = __fadd_rn(ss, __fmul_rn(v, v));
+#pragma unroll 4
+            for (int r = threadIdx.x; r < runs; r += kPrepThreads) {
+                const uint4 v = xq4d::ldcg_v4(x + (size_t)tk * p.k + 8 * (size_t)r);
+                const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const float lo = __uint_as_float(wd[h] << 16), hi = __uint_as_float(wd[h] & 0xFFFF0000u);
+                    ss = __fadd_rn(ss, __fmul_rn(lo, lo));
+                    ss = __fadd_rn(ss, __fmul_rn(hi, hi));
+                }
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-            if (lane == 0) sinv[w] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)p.k), p.eps)));
+            if (lane == 0) wsum[w] = ss;
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                float t = 0.f;
+                for (int i = 0; i < kPrepThreads / 32; i++) t = __fadd_rn(t, wsum[i]);
+                sinv[tk] = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)p.k), p.eps)));
+            }
+            __syncthreads();
         }
     }
     __syncthreads();
@@ -906,6 +924,10 @@ __device__ __forceinline__ bool consume_stage_w4a8(uint32_t stage, uint64_t *ful
     return true;
 }
 
+// W8: the chain holds W4A8 ops.  The W4A8 path is compiled only into that
+// instantiation: inside the register-capped fp16 kernel it cost the fp16 ops
+// 6 % (measured on B200, the 32-layer decode set).
+template <bool W8>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int2 *__restrict__ rng,
                   unsigned *__restrict__ done, const __grid_constant__ xq4_chain_p2p p2p)
@@ -1008,7 +1030,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                 // bf16 and the partials added in f32 in chunk order, as
                 // w4a8_kernel (the reference's w4u_read_c, main.rs:3066-3091)
                 float val[4] = {0.f, 0.f, 0.f, 0.f};
-                const int nst = op.w4a8 ? op.spr : 1;
+                const int nst = (W8 && op.w4a8) ? op.spr : 1;
                 for (int st = 0; st < nst; st++, rbl++) {
                     const int buf = rbl % kRedBufs;
                     const uint32_t use = (uint32_t)(rbl / kRedBufs);
@@ -1025,7 +1047,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                             float sum = 0.f;
 #pragma unroll
                             for (int w = 0; w < kConsumerWarps; w++) sum += rd[(size_t)w * 128 + oo];
-                            if (op.w4a8) {
+                            if (W8 && op.w4a8) {
                                 const float part = __bfloat162float(__float2bfloat16_rn(sum));
                                 val[j] = st == 0 ? part : val[j] + part;
                             } else {
@@ -1192,7 +1214,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
         const int tok = g < op.m ? g : 0;
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
                                              : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
-        const uint8_t *const qrow = op.w4a8 ? op.qx_img + (size_t)tok * op.kc * XQ4G_KCHUNK : nullptr;
+        const uint8_t *const qrow = (W8 && op.w4a8) ? op.qx_img + (size_t)tok * op.kc * XQ4G_KCHUNK : nullptr;
         int rb0, rb1;
         chain_range(rng, o, cta, G, rb0, rb1);
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
@@ -1219,7 +1241,7 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                 const uint32_t stage = ring_s + (uint32_t)slot * kChainStageBytes;
                 const bool whole = kc0 + kStageChunks <= op.kc;
                 bool ok;
-                if (op.w4a8)
+                if (W8 && op.w4a8)
                     ok = consume_stage_w4a8(stage, &full[slot], phase, kc0, op.kc, qrow, op.qx_tbl, warp, lane,
                                             acc[0]);
                 else
@@ -1250,12 +1272,12 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                     slot = 0;
                     phase ^= 1;
                 }
-                if (op.w4a8 && !handoff()) {
+                if (W8 && op.w4a8 && !handoff()) {
                     atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
                     return;
                 }
             }
-            if (!op.w4a8 && !handoff()) {  // row block complete
+            if (!(W8 && op.w4a8) && !handoff()) {  // row block complete
                 atomicOr(&g_xq4_fault, XQ4_FAULT_GEMV_FULL);
                 return;
             }
@@ -1367,18 +1389,30 @@ size_t xq4_gemv_chain_smem() { return kChainSmem; }
 
 // Set the chain kernel's shared-memory attribute on the current device and
 // check that its whole grid can be resident (its op waits need that).
-cudaError_t xq4_gemv_chain_prepare()
+// The chain kernels' shared-memory attribute, once per device.
+static cudaError_t chain_attrs()
 {
     static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmem);
+        cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kChainSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemv_chain_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kChainSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    if (!whole_grid_resident((const void *)gemv_chain_kernel, kThreads, kChainSmem,
-                             sm_count_of_current_device() * kCtasPerSm))
+    return cudaSuccess;
+}
+
+cudaError_t xq4_gemv_chain_prepare()
+{
+    if (cudaError_t e = chain_attrs(); e != cudaSuccess) return e;
+    const int grid = sm_count_of_current_device() * kCtasPerSm;
+    if (!whole_grid_resident((const void *)gemv_chain_kernel<false>, kThreads, kChainSmem, grid) ||
+        !whole_grid_resident((const void *)gemv_chain_kernel<true>, kThreads, kChainSmem, grid))
         return cudaErrorCooperativeLaunchTooLarge;
     return cudaSuccess;
 }
@@ -1387,7 +1421,7 @@ int xq4_gemv_chain_grid() { return sm_count_of_current_device() * kCtasPerSm; }
 
 cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid, unsigned *done,
                                   const xq4_chain_prep_dev *preps, int n_preps, const xq4_chain_p2p &p2p,
-                                  cudaStream_t st)
+                                  bool has_w4a8, cudaStream_t st)
 {
     if (n_preps > 0) {  // the fp16 images first; the chain's producers start meanwhile (PDL)
         cudaLaunchConfig_t pc = {};
@@ -1402,14 +1436,7 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const 
         cudaError_t e = cudaLaunchKernelEx(&pc, chain_prep_kernel, preps);
         if (e != cudaSuccess) return e;
     }
-    static std::atomic<bool> attr_set[64];  // zero-initialised; atomics: first launches may race across threads
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kChainSmem);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
+    if (cudaError_t e = chain_attrs(); e != cudaSuccess) return e;  // residency was checked at chain create
     cudaLaunchConfig_t cfg = {};
     // every CTA resident (the op waits need it; checked at chain create); the
     // grid the range table was built for
@@ -1422,7 +1449,8 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_chain_kernel, ops, n_ops, rng, done, p2p);
+    return has_w4a8 ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<true>, ops, n_ops, rng, done, p2p)
+                    : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<false>, ops, n_ops, rng, done, p2p);
 }
 
 // Read and clear this unit's fault word on the current device.

@@ -158,9 +158,10 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 // n_ops + 1 zeroed counters (left zeroed at the end of the launch).
 // `rng` holds each op's row-block range per CTA ([op][cta], grid CTAs;
 // xq4_chain_ranges), built for `grid` = xq4_gemv_chain_grid() at create.
+// has_w4a8: the chain holds W4A8 ops (the kernel instantiation with that path).
 cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid,
                                   unsigned *done, const struct xq4_chain_prep_dev *preps, int n_preps,
-                                  const struct xq4_chain_p2p &p2p, cudaStream_t st);
+                                  const struct xq4_chain_p2p &p2p, bool has_w4a8, cudaStream_t st);
 // CTAs of a chain launch on the current device.
 int xq4_gemv_chain_grid();
 size_t xq4_gemv_chain_smem();
