@@ -1,7 +1,9 @@
 """Generate the committed golden fixtures for the int4 path.
 
-Run in a container where the reference source is mounted (default
-/root/reference); the fixtures it writes are committed and the tests never
+Usage: python tests/golden/make_golden.py <reference source tree>
+
+Run where the reference source is mounted, giving its root as the one
+required argument; the fixtures it writes are committed and the tests never
 read the reference at run time.
 
 1. golden_<shape>.bin -- produced by the REFERENCE'S OWN functions
@@ -36,7 +38,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+REF = None  # the reference source tree, the required command-line argument
 sys.path.insert(0, str(HERE.parent.parent))
 from xnpu_b200 import synth  # noqa: E402
 
@@ -130,6 +132,10 @@ def l2_pack_py(q, s):
 
 
 def main():
+    global REF
+    if len(sys.argv) != 2 or not (Path(sys.argv[1]) / "tools" / "w4_import.py").is_file():
+        sys.exit("usage: make_golden.py <reference source tree (holding tools/w4_import.py)>")
+    REF = Path(sys.argv[1])
     spot_rows, write_golden, shapes = load_reference_functions()
     manifest = {"golden": {}, "kat": {}, "layouts": {}}
     golden_shapes = {name: (m, k, tsi) for name, (_parts, m, k, tsi) in shapes.items()}
