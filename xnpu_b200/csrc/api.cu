@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <limits.h>
 #include <string.h>
 #include <time.h>
 #include <unistd.h>
@@ -369,11 +370,10 @@ struct xq4_chain {
     xq4_device *dev;
     int ordinal;
     int n_ops, n_preps;
-    xq4_chain_op_dev *d_ops;  // one allocation: op table, n_ops + 1 completion counters,
-    unsigned *d_done;         // prep table, range table, fp16 images
-    xq4_chain_prep_dev *d_preps;
-    const int2 *d_rng;        // [op][cta] row-block ranges
-    int grid;                 // CTAs per launch (the range table's)
+    xq4_chain_op_dev *d_ops;  // one allocation: op table, segment counters, prep table,
+    xq4_chain_prep_dev *d_preps;  // plan (segment CTA counts, visit lists), fp16 images
+    xq4_chain_plan plan;
+    int grid;                 // CTAs per launch (the plan's)
     bool has_w4a8;            // some op runs in the W4A8 mode
     xq4_chain_p2p p2p;        // sharded ops' communicator (nranks 1: none)
     xq4_comm *comm;           // that communicator, or NULL
@@ -440,7 +440,6 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.shard = o.comm && p2p.nranks > 1;
         d.residual = (const uint16_t *)o.residual_dev;
         d.swiglu = o.swiglu != 0;
-        d.wait_parity = 0;
         if (o.residual_dev || o.swiglu || o.norm_w_dev) {
             if (o.comm && o.residual_dev) return xq4_fail(XQ4_EINVAL, "op %d: a residual epilogue on a sharded op", i);
             if ((o.residual_dev || o.swiglu) && o.out_dtype != XQ4_OUT_BF16)
@@ -462,17 +461,17 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
                                 inbox_words);
         }
     }
-    // the consumers' op barrier completes once per waiting op (op 0 never waits)
-    for (int i = 1, waits = 0; i < n_ops; i++)
-        if (tab[(size_t)i].wait_prev) tab[(size_t)i].wait_parity = waits++ & 1;
     // segments: a new one starts at op 0 and at every op that waits
-    for (int i = 0; i < n_ops;) {
+    std::vector<int> op_seg((size_t)n_ops);
+    int n_seg = 0;
+    for (int i = 0; i < n_ops; n_seg++) {
         int j = i + 1;
         while (j < n_ops && !tab[(size_t)j].wait_prev) j++;
         long long units = 0;
         for (int q = i; q < j; q++) {
             tab[(size_t)q].seg_start = units;
             units += (long long)tab[(size_t)q].nb * tab[(size_t)q].spr;
+            op_seg[(size_t)q] = n_seg;
         }
         for (int q = i; q < j; q++) tab[(size_t)q].seg_units = units;
         i = j;
@@ -496,7 +495,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     std::vector<int> op_prep((size_t)n_ops, -1);
     const auto align = [](size_t v) { return (v + 255) & ~(size_t)255; };
     const size_t tab_bytes = align(tab.size() * sizeof(xq4_chain_op_dev));
-    const size_t done_bytes = align(((size_t)n_ops + 1) * sizeof(unsigned));
+    const size_t done_bytes = align(((size_t)n_seg + 1) * sizeof(unsigned));
     size_t img_bytes = 0;
     for (int i = 0; i < n_ops; i++) {
         const xq4_chain_op &o = ops[i];
@@ -544,26 +543,43 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         op_prep[(size_t)i] = pi;
     }
     const size_t prep_bytes = align(preps.size() * sizeof(xq4_chain_prep_dev));
-    // Row-block range of every op for every CTA: CTA c owns the row blocks
-    // whose first stage falls in [c*U/G, (c+1)*U/G) of its segment's U
-    // stages (shares differ by at most one row block).
+    // The plan: CTA c owns the row blocks of op i whose first stage falls in
+    // [c*U/G, (c+1)*U/G) of its segment's U stages (shares differ by at most
+    // one row block); its visits are the ops where that is not empty.
     const int grid = xq4_gemv_chain_grid();
-    std::vector<int2> rng((size_t)n_ops * grid);
-    for (int i = 0; i < n_ops; i++) {
-        const xq4_chain_op_dev &d = tab[(size_t)i];
-        const auto first_at = [&](long long st) -> int {  // first row block starting at stage >= st
-            if (st <= 0) return 0;
-            const long long r = (st + d.spr - 1) / d.spr;
-            return r < d.nb ? (int)r : d.nb;
-        };
-        for (int c = 0; c < grid; c++) {
-            const long long lo = (long long)c * d.seg_units / grid - d.seg_start;
-            const long long hi = (long long)(c + 1) * d.seg_units / grid - d.seg_start;
-            rng[(size_t)i * grid + c] = make_int2(first_at(lo), first_at(hi));
+    std::vector<int4> visits;
+    std::vector<int> vstart((size_t)grid + 1);
+    std::vector<unsigned> seg_cnt((size_t)n_seg, 0u);
+    for (int c = 0; c < grid; c++) {
+        vstart[(size_t)c] = (int)visits.size();
+        for (int i = 0; i < n_ops; i++) {
+            const xq4_chain_op_dev &d = tab[(size_t)i];
+            const auto first_at = [&](long long st) -> int {  // first row block starting at stage >= st
+                if (st <= 0) return 0;
+                const long long r = (st + d.spr - 1) / d.spr;
+                return r < d.nb ? (int)r : d.nb;
+            };
+            const int rb0 = first_at((long long)c * d.seg_units / grid - d.seg_start);
+            const int rb1 = first_at((long long)(c + 1) * d.seg_units / grid - d.seg_start);
+            if (rb0 >= rb1) continue;
+            const int seg = op_seg[(size_t)i];
+            const bool first = visits.size() == (size_t)vstart[(size_t)c] || (visits.back().w >> 2) != seg;
+            if (first) {
+                seg_cnt[(size_t)seg]++;
+                if (visits.size() > (size_t)vstart[(size_t)c]) visits.back().w |= 2;  // last of its segment
+            }
+            visits.push_back(make_int4(i, rb0, rb1, seg << 2 | (first ? 1 : 0)));
         }
+        if (visits.size() > (size_t)vstart[(size_t)c]) visits.back().w |= 2;
     }
-    const size_t rng_bytes = align(rng.size() * sizeof(int2));
-    const size_t total = tab_bytes + done_bytes + prep_bytes + rng_bytes + img_bytes;
+    vstart[(size_t)grid] = (int)visits.size();
+    if (visits.size() > (size_t)INT_MAX / 2 || n_seg >= (1 << 29))
+        return xq4_fail(XQ4_EINVAL, "chain too large: %zu visits", visits.size());
+    const size_t seg_bytes = align((size_t)n_seg * sizeof(unsigned));
+    const size_t vstart_bytes = align(vstart.size() * sizeof(int));
+    const size_t visit_bytes = align(visits.size() * sizeof(int4));
+    const size_t plan_bytes = seg_bytes + vstart_bytes + visit_bytes;
+    const size_t total = tab_bytes + done_bytes + prep_bytes + plan_bytes + img_bytes;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
     void *mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, total);
@@ -571,7 +587,13 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         cudaGetLastError();
         return xq4_fail(XQ4_ENOMEM, "cudaMalloc(%zu) for the chain: %s", total, cudaGetErrorString(e));
     }
-    char *base = (char *)mem, *rng_d = base + tab_bytes + done_bytes + prep_bytes, *img = rng_d + rng_bytes;
+    char *base = (char *)mem, *plan_d = base + tab_bytes + done_bytes + prep_bytes, *img = plan_d + plan_bytes;
+    xq4_chain_plan plan{};
+    plan.seg_cnt = (const unsigned *)plan_d;
+    plan.vstart = (const int *)(plan_d + seg_bytes);
+    plan.visits = (const int4 *)(plan_d + seg_bytes + vstart_bytes);
+    plan.done = (unsigned *)(base + tab_bytes);
+    plan.n_seg = n_seg;
     std::vector<xq4_chain_prep_dev> ptab(preps.size());
     for (size_t q = 0; q < preps.size(); q++) {
         const prep_key &pk = preps[q];
@@ -616,7 +638,12 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     if (e == cudaSuccess && !ptab.empty())
         e = cudaMemcpy(base + tab_bytes + done_bytes, ptab.data(), ptab.size() * sizeof(xq4_chain_prep_dev),
                        cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(rng_d, rng.data(), rng.size() * sizeof(int2), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy((void *)plan.seg_cnt, seg_cnt.data(), seg_cnt.size() * sizeof(unsigned), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy((void *)plan.vstart, vstart.data(), vstart.size() * sizeof(int), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && !visits.empty())
+        e = cudaMemcpy((void *)plan.visits, visits.data(), visits.size() * sizeof(int4), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(mem);
@@ -625,9 +652,8 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     bool has_w4a8 = false;
     for (const xq4_chain_op_dev &d : tab) has_w4a8 = has_w4a8 || d.w4a8;
     xq4_chain *c = new (std::nothrow) xq4_chain{dev, dev->ordinal, n_ops, (int)preps.size(), (xq4_chain_op_dev *)mem,
-                                                (unsigned *)(base + tab_bytes),
                                                 (xq4_chain_prep_dev *)(base + tab_bytes + done_bytes),
-                                                (const int2 *)rng_d, grid, has_w4a8, p2p,
+                                                plan, grid, has_w4a8, p2p,
                                                 p2p.nranks > 1 ? comm : nullptr};
     if (!c) {
         cudaFree(mem);
@@ -656,8 +682,8 @@ extern "C" int xq4_chain_run(const xq4_chain *chain, void *stream)
     if (chain->comm)
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(chain->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
-                             chain->n_preps, chain->p2p, chain->has_w4a8, (cudaStream_t)stream),
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->plan, chain->grid, chain->d_preps, chain->n_preps, chain->p2p,
+                             chain->has_w4a8, (cudaStream_t)stream),
        "chain launch");
     return XQ4_OK;
 }
@@ -670,8 +696,8 @@ extern "C" int xq4_chain_submit(xq4_device *dev, const xq4_chain *chain, uint64_
     if (chain->comm)
         if (int rc = xq4_comm_check_usable(chain->comm)) return rc;
     CK(cudaSetDevice(dev->ordinal), "cudaSetDevice");
-    CK(xq4_launch_gemv_chain(chain->d_ops, chain->n_ops, chain->d_rng, chain->grid, chain->d_done, chain->d_preps,
-                             chain->n_preps, chain->p2p, chain->has_w4a8, dev->stream),
+    CK(xq4_launch_gemv_chain(chain->d_ops, chain->plan, chain->grid, chain->d_preps, chain->n_preps, chain->p2p,
+                             chain->has_w4a8, dev->stream),
        "chain launch");
     const uint64_t s = dev->last_seq + 1;
     CK(cudaEventRecord(dev->ring[s % kRing], dev->stream), "cudaEventRecord");

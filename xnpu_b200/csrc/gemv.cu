@@ -650,16 +650,18 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
 // One persistent launch over a list of GEMVs (m <= 8 each, bf16 path), the
 // B200 form of the reference's chained op submission (crates/xnpu-cli/src/
 // main.rs:1611-1635, and the projection stream of cmd_run_w4layer,
-// main.rs:2487-2499).  Same warp roles as gemv_kernel.  CTA c owns the same
-// share of every op's row blocks; the producer streams op after op through
-// one ring, so the next op's weights are already in flight while the
+// main.rs:2487-2499).  Same warp roles as gemv_kernel.  CTA c owns one
+// contiguous share of each segment's row blocks (its visits, below); the
+// producer streams visit after visit through one ring, so the next op's
+// weights are already in flight while the
 // consumers finish the current one, and the per-launch ramp and tail of
-// separate kernels happen once per chain.  An op marked wait_prev reads its
-// x only after every CTA has written the previous op's y: the reducers count
-// finished CTAs per op (release), one consumer thread per CTA waits for the
-// count (acquire, bounded) and releases the other consumer warps through a
-// named barrier.  x is read through L2 (ld.global.cg): it may have been
-// written earlier in the same launch.
+// separate kernels happen once per chain.  An op marked wait_prev starts a
+// segment and reads its x only after every CTA has written the previous
+// segment's outputs: the reducers count the CTAs done with each segment
+// (release), one consumer thread per CTA waits for the count (acquire,
+// bounded) and releases the other consumer warps through an mbarrier.  x is
+// then read through L2 (ld.global.cg): it may have been written earlier in
+// the same launch.
 #ifndef XQ4_CHAIN_STAGES
 #define XQ4_CHAIN_STAGES 4
 #endif
@@ -681,17 +683,14 @@ static_assert(kChainStageBytes % 128 == 0, "stage alignment");
 static_assert(kChainRingOff % 128 == 0, "ring alignment");
 static_assert((kChainSmem + 1024) * kCtasPerSm <= 228 * 1024, "kCtasPerSm chain CTAs per SM");
 
-// This CTA's row blocks [rb0, rb1) of op o: those whose first stage falls in
-// the CTA's share [cta*U/G, (cta+1)*U/G) of its segment's U stages.  The host
-// computes the table at chain create (xq4_chain_ranges), one int2 per (op,
-// CTA): working it out here would cost every warp four 64-bit divisions per
-// op.
-__device__ __forceinline__ void chain_range(const int2 *__restrict__ rng, int o, int cta, int G, int &rb0, int &rb1)
-{
-    const int2 r = __ldg(rng + (size_t)o * G + cta);
-    rb0 = r.x;
-    rb1 = r.y;
-}
+// A CTA's work is its list of visits, built at chain create: one per op in
+// which it owns row blocks, {op, rb0, rb1, seg << 2 | last << 1 | first}
+// (first / last: the CTA's first / last visit in segment seg).  CTA c owns the
+// row blocks whose first stage falls in its share [c*U/G, (c+1)*U/G) of its
+// segment's U stages, so in a long chain of independent ops it visits one or
+// two ops: walking every op instead (a table load, and for the reducer a
+// release, per op) delayed the last CTAs' first stage by microseconds per op.
+constexpr int kVisitFirst = 1, kVisitLast = 2;
 
 // Prep for the chain's fp16 path: one CTA per activation converts it as the
 // single-op GEMV's fp16 staging does (the same per-token power of two, the
@@ -929,8 +928,8 @@ __device__ __forceinline__ bool consume_stage_w4a8(uint32_t stage, uint64_t *ful
 // 6 % (measured on B200, the 32-layer decode set).
 template <bool W8>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
-gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int2 *__restrict__ rng,
-                  unsigned *__restrict__ done, const __grid_constant__ xq4_chain_p2p p2p)
+gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constant__ xq4_chain_plan plan,
+                  const __grid_constant__ xq4_chain_p2p p2p)
 {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -943,6 +942,8 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
+    const int v0 = __ldg(plan.vstart + cta), v1 = __ldg(plan.vstart + cta + 1);  // this CTA's visits
+    unsigned *const done = plan.done;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kChainStages; s++) {
@@ -965,10 +966,10 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
             uint32_t phase = 0;
             bool alive = true;
             bool prep_done = false;  // the x and table slices are the prep kernel's output
-            for (int o = 0; o < n_ops && alive; o++) {
-                const xq4_chain_op_dev op = ops[o];
-                int rb0, rb1;
-                chain_range(rng, o, cta, G, rb0, rb1);
+            for (int v = v0; v < v1 && alive; v++) {
+                const int4 vi = __ldg(plan.visits + v);
+                const xq4_chain_op_dev op = ops[vi.x];
+                const int rb0 = vi.y, rb1 = vi.z;
                 for (int rb = rb0; rb < rb1 && alive; rb++) {
                     for (int kc0 = 0; kc0 < op.kc; kc0 += kStageChunks, i++) {
                         if (i >= kChainStages && !xq4d::mbar_wait(&empty[slot], phase ^ 1)) {
@@ -1012,12 +1013,12 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
         const size_t half = p2p.nranks > 1 ? (size_t)(e & 1u) * p2p.half_words : 0;
         // a poisoned communicator (an earlier call gave up on a peer): local rows only
         const bool xchg = p2p.nranks > 1 && p2p_usable(p2p.poison, p2p.rank, lane);
-        int rbl = 0, pend = 0;  // ops [pend, o] may hold sharded rows whose peer copies are not in y yet
+        int rbl = 0, pend = v0;  // visits [pend, v] may hold sharded rows whose peer copies are not in y yet
         bool alive = true;
-        for (int o = 0; o < n_ops; o++) {
-            const xq4_chain_op_dev op = ops[o];
-            int rb0, rb1;
-            chain_range(rng, o, cta, G, rb0, rb1);
+        for (int v = v0; v < v1; v++) {
+            const int4 vi = __ldg(plan.visits + v);
+            const xq4_chain_op_dev op = ops[vi.x];
+            const int rb0 = vi.y, rb1 = vi.z, seg = vi.w >> 2;
             // output row stride and this rank's first output row (a SwiGLU op
             // writes one value per row pair)
             const size_t ystride = (size_t)(op.shard ? op.n_total : op.n) >> (op.swiglu ? 1 : 0);
@@ -1120,19 +1121,20 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                     }
                 }
             }
-            // Before an op that waits for this one (or at the end), the
-            // peers' rows of this CTA's ranges of the pending sharded ops go
-            // from the inbox into y.  Each peer's CTA with this index
-            // computed them (equal shards, equal chains), and every CTA sends
-            // its words before it waits, so no wait depends on a waiting CTA.
-            if (xchg && (o + 1 == n_ops || ops[o + 1].wait_prev)) {
+            if (!(vi.w & kVisitLast)) continue;
+            // The CTA's last visit in its segment: the peers' rows of its
+            // ranges of the segment's sharded ops go from the inbox into y.
+            // Each peer's CTA with this index computed them (equal shards,
+            // equal chains), and every CTA sends its words before it waits,
+            // so no wait depends on a waiting CTA.
+            if (xchg) {
                 const uint64_t t0 = xq4d::global_ns();
                 bool ok = alive;
-                for (int s = pend; ok && s <= o; s++) {
-                    const xq4_chain_op_dev so = ops[s];
+                for (int s = pend; ok && s <= v; s++) {
+                    const int4 si = __ldg(plan.visits + s);
+                    const xq4_chain_op_dev so = ops[si.x];
                     if (!so.shard) continue;
-                    int s0, s1;
-                    chain_range(rng, s, cta, G, s0, s1);
+                    const int s0 = si.y, s1 = si.z;
                     // this CTA's output rows of the op (row pairs for SwiGLU;
                     // row blocks hold 16 rows, so a range never splits a pair)
                     const int sh = so.swiglu ? 1 : 0;
@@ -1147,14 +1149,14 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                         const int tok = rem / span, row = r0 + (rem - tok * span);
                         const int q = qi < p2p.rank ? qi : qi + 1;
                         const size_t idx = (size_t)tok * stride + (size_t)q * ns + row;
-                        unsigned long long v = xq4d::ld_sys_u64(in + idx);
-                        while ((unsigned)(v >> 32) != e) {
+                        unsigned long long w = xq4d::ld_sys_u64(in + idx);
+                        while ((unsigned)(w >> 32) != e) {
                             if (xq4d::global_ns() - t0 > 2000000000ull) {
                                 ok = false;
                                 break;
                             }
                             __nanosleep(32);
-                            v = xq4d::ld_sys_u64(in + idx);
+                            w = xq4d::ld_sys_u64(in + idx);
                         }
                         if (!ok) {
                             atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
@@ -1162,22 +1164,23 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
                             break;
                         }
                         if (so.out_f32)
-                            reinterpret_cast<uint32_t *>(so.y)[idx] = (uint32_t)v;
+                            reinterpret_cast<uint32_t *>(so.y)[idx] = (uint32_t)w;
                         else
-                            reinterpret_cast<uint16_t *>(so.y)[idx] = (uint16_t)v;
+                            reinterpret_cast<uint16_t *>(so.y)[idx] = (uint16_t)w;
                     }
                 }
-                pend = o + 1;
             }
-            // this CTA's rows of op o are written (the warp barrier orders
-            // every lane's stores before lane 0's release)
+            pend = v + 1;
+            // this CTA's rows of the segment are written (the warp barrier
+            // orders every lane's stores before lane 0's release); no
+            // segment waits for the last one
             __syncwarp();
-            if (lane == 0) xq4d::red_release_gpu_add(&done[o], 1u);
+            if (lane == 0 && seg + 1 < plan.n_seg) xq4d::red_release_gpu_add(&done[seg], 1u);
         }
         // the last CTA out leaves the counters zeroed for the next launch and
         // advances the inbox epoch (every CTA read it before counting here)
-        if (lane == 0 && atomicAdd(&done[n_ops], 1u) == (unsigned)G - 1) {
-            for (int o = 0; o <= n_ops; o++) done[o] = 0u;
+        if (lane == 0 && atomicAdd(&done[plan.n_seg], 1u) == (unsigned)G - 1) {
+            for (int q = 0; q <= plan.n_seg; q++) done[q] = 0u;
             if (p2p.nranks > 1) *reinterpret_cast<volatile unsigned *>(p2p.epoch) = e;
         }
         return;
@@ -1190,17 +1193,22 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
     const uint32_t xs[1] = {0u};
     float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
     int slot = 0, rbl = 0;
-    uint32_t phase = 0;
-    for (int o = 0; o < n_ops; o++) {
-        const xq4_chain_op_dev op = ops[o];
-        if (op.wait_prev && o > 0) {
-            // warp 0 sees every CTA's count (acquire), then the consumer
-            // warps meet on an mbarrier (release / acquire within the CTA):
-            // a bounded wait, so a warp that gave up earlier cannot hold the
-            // others forever
+    uint32_t phase = 0, waits = 0;
+    for (int v = v0; v < v1; v++) {
+        const int4 vi = __ldg(plan.visits + v);
+        const xq4_chain_op_dev op = ops[vi.x];
+        const int seg = vi.w >> 2;
+        if ((vi.w & kVisitFirst) && seg > 0) {
+            // The CTA's first visit in a segment after the first: every CTA
+            // that visits the previous segment is done with it (and, through
+            // the waits those CTAs passed, with every earlier segment).  Warp
+            // 0 sees the count (acquire), then the consumer warps meet on an
+            // mbarrier (release / acquire within the CTA): a bounded wait, so
+            // a warp that gave up earlier cannot hold the others forever.
             if (warp == 0 && lane == 0) {
                 const uint64_t t0 = xq4d::global_ns();
-                while (xq4d::ld_acquire_gpu_u32(&done[o - 1]) < (unsigned)G) {
+                const unsigned want = __ldg(plan.seg_cnt + seg - 1);
+                while (xq4d::ld_acquire_gpu_u32(&done[seg - 1]) < want) {
                     if (xq4d::global_ns() - t0 > 2000000000ull) {
                         atomicOr(&g_xq4_fault, XQ4_FAULT_CHAIN_WAIT);
                         break;
@@ -1209,14 +1217,14 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, int n_ops, const int
             }
             __syncwarp();
             if (lane == 0) xq4d::mbar_arrive(op_bar);
-            if (!xq4d::mbar_wait(op_bar, (uint32_t)op.wait_parity)) atomicOr(&g_xq4_fault, XQ4_FAULT_CHAIN_WAIT);
+            if (!xq4d::mbar_wait(op_bar, waits & 1u)) atomicOr(&g_xq4_fault, XQ4_FAULT_CHAIN_WAIT);
+            waits++;
         }
         const int tok = g < op.m ? g : 0;
         const uint16_t *const xr[1] = {op.xh ? op.xh_img + (size_t)tok * op.kc * XQ4G_KCHUNK
                                              : reinterpret_cast<const uint16_t *>(op.x) + (size_t)tok * op.k};
         const uint8_t *const qrow = (W8 && op.w4a8) ? op.qx_img + (size_t)tok * op.kc * XQ4G_KCHUNK : nullptr;
-        int rb0, rb1;
-        chain_range(rng, o, cta, G, rb0, rb1);
+        const int rb0 = vi.y, rb1 = vi.z;
         const bool k_whole = (op.k % XQ4G_KCHUNK) == 0;
         const float hs = op.xh ? 0.0625f : 1.f;  // fp16 path: rows g+8 summed 16 * c
         // the warp's partials to buffer rbl % kRedBufs: per row block, or per
@@ -1419,7 +1427,7 @@ cudaError_t xq4_gemv_chain_prepare()
 
 int xq4_gemv_chain_grid() { return sm_count_of_current_device() * kCtasPerSm; }
 
-cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid, unsigned *done,
+cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, const xq4_chain_plan &plan, int grid,
                                   const xq4_chain_prep_dev *preps, int n_preps, const xq4_chain_p2p &p2p,
                                   bool has_w4a8, cudaStream_t st)
 {
@@ -1449,8 +1457,8 @@ cudaError_t xq4_launch_gemv_chain(const xq4_chain_op_dev *ops, int n_ops, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return has_w4a8 ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<true>, ops, n_ops, rng, done, p2p)
-                    : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<false>, ops, n_ops, rng, done, p2p);
+    return has_w4a8 ? cudaLaunchKernelEx(&cfg, gemv_chain_kernel<true>, ops, plan, p2p)
+                    : cudaLaunchKernelEx(&cfg, gemv_chain_kernel<false>, ops, plan, p2p);
 }
 
 // Read and clear this unit's fault word on the current device.

@@ -86,13 +86,25 @@ struct xq4_chain_op_dev {
     // this rank's pairs from row_off/2).
     const uint16_t *residual;
     int swiglu;
-    int wait_parity;      // phase parity of the consumers' op barrier at this op (waiting ops before it, mod 2)
     // W4A8 (the reference's NPU numerics): x quantized by the prep to int8
     // per 32-K group; per group one integer MMA, times s_w * d_x; each stage
     // (2048 K) is one chunk partial, rounded to bf16 and summed in f32.
     int w4a8;
     const uint8_t *qx_img;     // [m][kc*64] int8, bytes 0,2,1,3 within each 4 (the MMA's slot order)
     const int2 *qx_tbl;        // [groups][8 tokens]: {-8 * sum(q_x), bits of f32(d_x)}
+};
+
+// The chain's work plan, built at chain create.  A segment is a run of ops
+// of which only the first waits for its predecessor.  Each CTA has a list of
+// visits, one per op in which it owns row blocks: {op, rb0, rb1, seg << 2 |
+// last << 1 | first}, first / last marking its first / last visit in the
+// segment.
+struct xq4_chain_plan {
+    const int4 *visits;
+    const int *vstart;        // [grid + 1]: CTA c's visits are [vstart[c], vstart[c + 1])
+    const unsigned *seg_cnt;  // [n_seg]: CTAs with a visit in the segment
+    unsigned *done;           // [n_seg + 1]: CTAs done with the segment; [n_seg]: CTAs out
+    int n_seg;
 };
 
 // The chain's communicator side (nranks == 1: no sharded op).
@@ -159,8 +171,8 @@ cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, in
 // `rng` holds each op's row-block range per CTA ([op][cta], grid CTAs;
 // xq4_chain_ranges), built for `grid` = xq4_gemv_chain_grid() at create.
 // has_w4a8: the chain holds W4A8 ops (the kernel instantiation with that path).
-cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, int n_ops, const int2 *rng, int grid,
-                                  unsigned *done, const struct xq4_chain_prep_dev *preps, int n_preps,
+cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, const struct xq4_chain_plan &plan, int grid,
+                                  const struct xq4_chain_prep_dev *preps, int n_preps,
                                   const struct xq4_chain_p2p &p2p, bool has_w4a8, cudaStream_t st);
 // CTAs of a chain launch on the current device.
 int xq4_gemv_chain_grid();
