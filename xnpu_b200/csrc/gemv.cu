@@ -316,6 +316,44 @@ __device__ __forceinline__ bool p2p_usable(const xq4_p2p_poison &p, int rank, in
     return v == 0u;
 }
 
+// Copy the peers' words i = lane, lane + 32, ... < total_w of an inbox
+// (value bits | epoch << 32) into y (bf16 or f32 values) once each carries
+// epoch e; idx_of(i) gives word i's index in the inbox half and in y (the same
+// [tok][n_total] position; below XQ4_FUSED_MAX_VALUES).  Eight loads per lane
+// are in flight together: one at a time, the loop cost a round trip to
+// memory per 32 words.  False when a word is still stale after the bounded
+// wait (2 s from t0).
+template <class IdxF>
+__device__ __forceinline__ bool gather_inbox(const unsigned long long *in, unsigned e, int total_w, int lane,
+                                             uint64_t t0, bool out_f32, void *y, IdxF idx_of)
+{
+    constexpr int kBatch = 8;
+    for (int i0 = lane; i0 < total_w; i0 += 32 * kBatch) {
+        int idx[kBatch];
+        unsigned long long w[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            const int i = i0 + 32 * j;
+            idx[j] = i < total_w ? idx_of(i) : -1;
+            w[j] = idx[j] >= 0 ? xq4d::ld_sys_u64(in + idx[j]) : 0ull;
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; j++) {
+            if (idx[j] < 0) continue;
+            while ((unsigned)(w[j] >> 32) != e) {
+                if (xq4d::global_ns() - t0 > 2000000000ull) return false;
+                __nanosleep(32);
+                w[j] = xq4d::ld_sys_u64(in + idx[j]);
+            }
+            if (out_f32)
+                reinterpret_cast<uint32_t *>(y)[idx[j]] = (uint32_t)w[j];
+            else
+                reinterpret_cast<uint16_t *>(y)[idx[j]] = (uint16_t)w[j];
+        }
+    }
+    return true;
+}
+
 template <int NT, bool XH, bool P2P>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
@@ -453,30 +491,15 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             const unsigned long long *in = p2p.inbox[p2p.rank] + half;
             const int per_peer = m * span, total_w = (p2p.nranks - 1) * per_peer;
             const uint64_t t0 = xq4d::global_ns();
-            bool ok = alive && xchg;
-            for (int i = lane; ok && i < total_w; i += 32) {
-                const int qi = i / per_peer, rem = i - qi * per_peer;
-                const int tok = rem / span, row = r0 + (rem - tok * span);
-                const int q = qi < p2p.rank ? qi : qi + 1;
-                const size_t idx = (size_t)tok * p2p.n_total + (size_t)q * n + row;
-                unsigned long long v = xq4d::ld_sys_u64(in + idx);
-                while ((unsigned)(v >> 32) != e) {
-                    if (xq4d::global_ns() - t0 > 2000000000ull) {
-                        ok = false;
-                        break;
-                    }
-                    __nanosleep(32);
-                    v = xq4d::ld_sys_u64(in + idx);
-                }
-                if (!ok) {
-                    atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
-                    p2p_poison(p2p.poison, p2p.nranks);
-                    break;
-                }
-                if (out_f32)
-                    reinterpret_cast<uint32_t *>(y)[idx] = (uint32_t)v;
-                else
-                    reinterpret_cast<uint16_t *>(y)[idx] = (uint16_t)v;
+            if (alive && xchg &&
+                !gather_inbox(in, e, total_w, lane, t0, out_f32 != 0, y, [&](int i) {
+                    const int qi = i / per_peer, rem = i - qi * per_peer;
+                    const int tok = rem / span, row = r0 + (rem - tok * span);
+                    const int q = qi < p2p.rank ? qi : qi + 1;
+                    return tok * p2p.n_total + q * n + row;
+                })) {
+                atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                p2p_poison(p2p.poison, p2p.nranks);
             }
             // the last CTA of this launch advances the epoch: every CTA has
             // read it by the time it counts itself here
@@ -1144,29 +1167,15 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
                     const size_t stride = (size_t)so.n_total >> sh;
                     const unsigned long long *in = p2p.inbox[p2p.rank] + half + so.inbox_off;
                     const int per_peer = so.m * span, total_w = (p2p.nranks - 1) * per_peer;
-                    for (int i = lane; ok && i < total_w; i += 32) {
+                    ok = gather_inbox(in, e, total_w, lane, t0, so.out_f32 != 0, so.y, [&](int i) {
                         const int qi = i / per_peer, rem = i - qi * per_peer;
                         const int tok = rem / span, row = r0 + (rem - tok * span);
                         const int q = qi < p2p.rank ? qi : qi + 1;
-                        const size_t idx = (size_t)tok * stride + (size_t)q * ns + row;
-                        unsigned long long w = xq4d::ld_sys_u64(in + idx);
-                        while ((unsigned)(w >> 32) != e) {
-                            if (xq4d::global_ns() - t0 > 2000000000ull) {
-                                ok = false;
-                                break;
-                            }
-                            __nanosleep(32);
-                            w = xq4d::ld_sys_u64(in + idx);
-                        }
-                        if (!ok) {
-                            atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
-                            p2p_poison(p2p.poison, p2p.nranks);
-                            break;
-                        }
-                        if (so.out_f32)
-                            reinterpret_cast<uint32_t *>(so.y)[idx] = (uint32_t)w;
-                        else
-                            reinterpret_cast<uint16_t *>(so.y)[idx] = (uint16_t)w;
+                        return (int)(tok * stride) + q * ns + row;
+                    });
+                    if (!ok) {
+                        atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+                        p2p_poison(p2p.poison, p2p.nranks);
                     }
                 }
             }
