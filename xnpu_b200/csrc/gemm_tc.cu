@@ -254,6 +254,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool failed = false;
+    // The next launch on the stream may start its prologue and weight loads
+    // now (programmatic dependent launch); x (read below) and y (written in
+    // the epilogue) wait for the previous launch to complete.
+    xq4d::grid_dep_launch();
 
     // Ring positions advance incrementally (slot, phase parity): no integer
     // division by the runtime ring depths in the loops.
@@ -283,6 +287,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
         }
     } else if (warp == kXWarp) {  // ------------------------------ activation producer
         if (lane == 0) {
+            xq4d::grid_dep_wait();
             const uint32_t bytes = (uint32_t)x_tile_bytes(bn);
             int s = 0, issued = 0;
             uint32_t ph = 0;
@@ -395,6 +400,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     // [h*bn/2, (h+1)*bn/2) (tokens), h = w / 4.
     const bool epi = warp < kDqWarps;
     if (epi) {
+        xq4d::grid_dep_wait();
         if (!xq4d::mbar_wait(accf, 0)) failed = true;
         tc_fence_after();
         const int q4 = warp & 3, h = warp >> 2;
@@ -431,12 +437,29 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             const int c_lo = (int)((long long)z * bn / S), c_hi = (int)((long long)(z + 1) * bn / S);
             const int f = threadIdx.x & (kTileN - 1), feat = rb0 * XQ4G_ROWS + f;
             const uint32_t part_s = xq4d::smem_u32(part);
-            for (int c = c_lo + (threadIdx.x >> 7); c < c_hi; c += kDqThreads / kTileN) {
-                const uint32_t off = (uint32_t)((c * kTileN + f) * 4);
-                float sum = 0.f;
-                for (int r = 0; r < S; r++) sum += ld_cluster_f32(cluster_map(part_s + off, (uint32_t)r));
-                const int tok = m0 + c;
-                if (!failed && tok < m && feat < n) store_out(y, out_f32, (size_t)tok * n + feat, sum);
+            // four columns' S partials in flight per thread, each column's
+            // summed in rank order
+            constexpr int kCols = 4, kStep = kDqThreads / kTileN;
+            for (int c0 = c_lo + (threadIdx.x >> 7); c0 < c_hi; c0 += kCols * kStep) {
+                float v[kCols][kMaxSplit];
+#pragma unroll
+                for (int j = 0; j < kCols; j++) {
+                    const int c = c0 + j * kStep;
+                    const uint32_t off = (uint32_t)((c * kTileN + f) * 4);
+#pragma unroll
+                    for (int r = 0; r < kMaxSplit; r++)
+                        v[j][r] = (c < c_hi && r < S) ? ld_cluster_f32(cluster_map(part_s + off, (uint32_t)r)) : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < kCols; j++) {
+                    const int c = c0 + j * kStep;
+                    float sum = 0.f;
+#pragma unroll
+                    for (int r = 0; r < kMaxSplit; r++)
+                        if (r < S) sum += v[j][r];
+                    const int tok = m0 + c;
+                    if (!failed && c < c_hi && tok < m && feat < n) store_out(y, out_f32, (size_t)tok * n + feat, sum);
+                }
             }
         }
         asm volatile("bar.sync 1, %0;" ::"r"(kThreads) : "memory");
@@ -550,13 +573,15 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = S;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = S;
     cfg.attrs = attr;
-    cfg.numAttrs = S > 1 ? 1 : 0;
+    cfg.numAttrs = S > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, D, S, y, out_f32);
 }
 
