@@ -53,8 +53,9 @@ SHARDED = ("gateup",)  # column-sharded over ranks, its SwiGLU intermediate gath
 #   ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum
 #       --clock-control none -k regex:gemv_chain --csv python bench.py --layers 4
 #       --steps 1 --warmup 3 --skip-e2e --skip-lmhead --skip-configs --no-cpu-baseline
-# (a 4-layer chain's bytes / 4; every layer has the same shapes).
-CHAIN_DRAM_PER_LAYER = 3929139200 // 32
+# (a 4-layer chain's steady-state bytes, 492,145,408, / 4; every layer has the
+# same shapes).
+CHAIN_DRAM_PER_LAYER = 492145408 // 4
 LMHEAD = (128256, 4096)
 METRIC = "decode tok/s, 8B-shaped int4 linear set (32 layers, batch 1)"
 DTYPE = "int4 weights (u4 codes, bf16 scales), bf16 x, f32 accumulate"
