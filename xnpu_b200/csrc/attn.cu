@@ -50,7 +50,10 @@ constexpr int kKStride = kHd + 2; // K row stride in shared memory (bf16): rows 
 constexpr int kMaxGroup = 8;      // q heads per kv head
 constexpr int kMaxSpan = 384;     // positions per CTA (its K and V rows and scores in shared memory)
 constexpr int kMaxSplits = 64;    // splits per kv head (the merge covers them in two lane rounds)
-constexpr int kMinSpan = 64;      // positions a split takes before the token uses another split (measured)
+#ifndef XQ4_ATTN_MIN_SPAN
+#define XQ4_ATTN_MIN_SPAN 64
+#endif
+constexpr int kMinSpan = XQ4_ATTN_MIN_SPAN;  // positions a split takes before the token uses another split (measured)
 // One split's partial of one head in the workspace: max, sum, two pad words
 // (so that acc starts 16 bytes in), acc[128]; 528 bytes, a multiple of 16.
 constexpr int kRec = 4 + kHd;
@@ -122,13 +125,43 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src)
 {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(xq4d::smem_u32(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ void cp_async4(void *dst, const void *src)
-{
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(xq4d::smem_u32(dst)), "l"(src) : "memory");
-}
 __device__ __forceinline__ void cp_async_wait_all()
 {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// Scores of rows tb + lane + 32 u (u < U) of the span against q: each over j
+// ascending (d = sum_j k[t][j] * q[j], main.rs:5006-5011), U independent
+// sums per lane; rows past the span read the last row and are dropped.
+template <int U>
+__device__ __forceinline__ void score_rows(const float *q, const uint16_t *kt, int tb, int nt, int lane, float rs,
+                                           float *scrow, float &m)
+{
+    float d[U];
+    const uint32_t *kr[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        d[u] = 0.f;
+        kr[u] = reinterpret_cast<const uint32_t *>(kt + min(tb + lane + 32 * u, nt - 1) * kKStride);
+    }
+    for (int j2 = 0; j2 < kHd / 2; j2++) {
+        const float q0 = q[2 * j2], q1 = q[2 * j2 + 1];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const uint32_t w = kr[u][j2];
+            d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w << 16), q0));
+            d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w & 0xFFFF0000u), q1));
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const int t = tb + lane + 32 * u;
+        if (t < nt) {
+            const float dv = __fdiv_rn(d[u], rs);
+            scrow[t] = dv;
+            m = fmaxf(m, dv);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -166,19 +199,42 @@ attn_decode_kernel(const attn_params p)
     const float *cs = p.rope ? p.rope + (size_t)pos * kHd : nullptr;
 
     // every K and V row of the span in flight at once (the token's own row,
-    // position pos, comes from this kernel instead); K rows land at a padded
-    // stride, so in 4-byte pieces
-    {
-        const size_t base = ((size_t)kv * p.cache_seq + t0) * kHd;
-        for (int i = threadIdx.x; i < nt * (kHd / 8); i += kThreads) {  // V: 16-byte pieces
-            const int r = i / (kHd / 8), c = i % (kHd / 8);
-            if (t0 + r != pos) cp_async16(vt + r * kHd + 8 * c, p.vc + base + (size_t)r * kHd + 8 * c);
-        }
-        for (int i = threadIdx.x; i < nt * (kHd / 2); i += kThreads) {  // K: 4-byte pieces
-            const int r = i / (kHd / 2), c = i % (kHd / 2);
-            if (t0 + r != pos) cp_async4(kt + r * kKStride + 2 * c, p.kc + base + (size_t)r * kHd + 2 * c);
-        }
+    // position pos, comes from this kernel instead): V by 16-byte
+    // asynchronous copies, K by 16-byte loads into registers (its rows land
+    // at a padded stride, 4-byte aligned; 4-byte asynchronous copies ran at a
+    // few GB/s per CTA), stored once the q heads are rotated
+    const size_t base = ((size_t)kv * p.cache_seq + t0) * kHd;
+    for (int i = threadIdx.x; i < nt * (kHd / 8); i += kThreads) {
+        const int r = i / (kHd / 8), c = i % (kHd / 8);
+        if (t0 + r != pos) cp_async16(vt + r * kHd + 8 * c, p.vc + base + (size_t)r * kHd + 8 * c);
     }
+    // K in batches of 64 rows (8 pieces per thread); the first batch's loads
+    // are in flight while the q heads are rotated
+    constexpr int kKBatch = 8;
+    const int kpieces = nt * (kHd / 8);
+    uint4 kreg[kKBatch];
+    const auto k_load = [&](int b0) {
+#pragma unroll
+        for (int u = 0; u < kKBatch; u++) {
+            const int i = b0 + threadIdx.x + u * kThreads, r = i / (kHd / 8), c = i % (kHd / 8);
+            if (i < kpieces && t0 + r != pos)
+                kreg[u] = __ldcs(reinterpret_cast<const uint4 *>(p.kc + base + (size_t)r * kHd + 8 * c));
+        }
+    };
+    const auto k_store = [&](int b0) {
+#pragma unroll
+        for (int u = 0; u < kKBatch; u++) {
+            const int i = b0 + threadIdx.x + u * kThreads, r = i / (kHd / 8), c = i % (kHd / 8);
+            if (i < kpieces && t0 + r != pos) {
+                uint32_t *d = reinterpret_cast<uint32_t *>(kt + r * kKStride + 8 * c);
+                d[0] = kreg[u].x;
+                d[1] = kreg[u].y;
+                d[2] = kreg[u].z;
+                d[3] = kreg[u].w;
+            }
+        }
+    };
+    k_load(0);
     // q heads of this group: RoPE + norm, kept in f32 (while the rows land)
     for (int hg = warp; hg < G; hg += kWarps)
         rope_norm_head(p.qkv + (size_t)(kv * G + hg) * kHd, cs, p.q_norm, tmp + warp * kHd, qf + hg * kHd, lane);
@@ -196,45 +252,28 @@ attn_decode_kernel(const attn_params p)
             p.vc[row + j] = vr[j];
         }
     }
+    k_store(0);
+    for (int b0 = kKBatch * kThreads; b0 < kpieces; b0 += kKBatch * kThreads) {
+        k_load(b0);
+        k_store(b0);
+    }
     cp_async_wait_all();
     __syncthreads();
 
     const float rs = sqrtf(128.f);  // (128f32).sqrt(): exact to f32 rounding
     float mx[kMaxGroup / kWarps];
     for (int i = 0; i < kMaxGroup / kWarps; i++) mx[i] = -INFINITY;
-    // pass 1: the scores; lane l takes positions l, l+32, ... of the span,
-    // four at a time (independent sums), each over j ascending
-    // (d = sum_j k[t][j] * q[j], main.rs:5006-5011)
+    // pass 1: the scores; lane l takes positions l, l+32, ... of the span
     for (int hg = warp, i = 0; hg < G; hg += kWarps, i++) {
         const float *q = qf + hg * kHd;
         float m = -INFINITY;
-        for (int tb = 0; tb < nt; tb += 128) {
-            float d[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t *kr[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) {  // rows past the span read the last row; their sums are dropped
-                const int t = min(tb + lane + 32 * u, nt - 1);
-                kr[u] = reinterpret_cast<const uint32_t *>(kt + t * kKStride);
-            }
-            for (int j2 = 0; j2 < kHd / 2; j2++) {
-                const float q0 = q[2 * j2], q1 = q[2 * j2 + 1];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint32_t w = kr[u][j2];
-                    d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w << 16), q0));
-                    d[u] = __fadd_rn(d[u], __fmul_rn(__uint_as_float(w & 0xFFFF0000u), q1));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int t = tb + lane + 32 * u;
-                if (t < nt) {
-                    const float dv = __fdiv_rn(d[u], rs);
-                    sc[hg * span + t] = dv;
-                    m = fmaxf(m, dv);
-                }
-            }
+        int tb = 0;  // rows of 128, then of 64 and 32: no lane sums a row past the span twice over
+        for (; nt - tb > 64; tb += 128) score_rows<4>(q, kt, tb, nt, lane, rs, sc + hg * span, m);
+        if (nt - tb > 32) {
+            score_rows<2>(q, kt, tb, nt, lane, rs, sc + hg * span, m);
+            tb += 64;
         }
+        if (nt - tb > 0) score_rows<1>(q, kt, tb, nt, lane, rs, sc + hg * span, m);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         mx[i] = m;
@@ -300,16 +339,26 @@ attn_decode_kernel(const attn_params p)
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) L = __fadd_rn(L, __shfl_xor_sync(0xffffffffu, L, o));
-        // sum_s f_s acc_s: every lane's 4 dims, the splits' loads in flight together
+        // sum_s f_s acc_s, s ascending: every lane's 4 dims, sixteen splits'
+        // loads in flight together (a few at a time cost a round trip each)
         float o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int sp = 0; sp < used; sp++) {
-            const float fs = __shfl_sync(0xffffffffu, f[sp >> 5], sp & 31);
-            const float4 a = __ldcg(reinterpret_cast<const float4 *>(w + (size_t)sp * kRec + kRecAcc + 4 * lane));
-            o[0] = __fadd_rn(o[0], __fmul_rn(a.x, fs));
-            o[1] = __fadd_rn(o[1], __fmul_rn(a.y, fs));
-            o[2] = __fadd_rn(o[2], __fmul_rn(a.z, fs));
-            o[3] = __fadd_rn(o[3], __fmul_rn(a.w, fs));
+        for (int sp0 = 0; sp0 < used; sp0 += 16) {
+            float4 a[16];
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                a[j] = sp0 + j < used
+                           ? __ldcg(reinterpret_cast<const float4 *>(w + (size_t)(sp0 + j) * kRec + kRecAcc + 4 * lane))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const int sp = sp0 + j;
+                if (sp >= used) break;
+                const float fs = __shfl_sync(0xffffffffu, f[sp >> 5], sp & 31);
+                o[0] = __fadd_rn(o[0], __fmul_rn(a[j].x, fs));
+                o[1] = __fadd_rn(o[1], __fmul_rn(a[j].y, fs));
+                o[2] = __fadd_rn(o[2], __fmul_rn(a[j].z, fs));
+                o[3] = __fadd_rn(o[3], __fmul_rn(a[j].w, fs));
+            }
         }
         uint16_t *out = p.out + (size_t)(kv * G + hg) * kHd + 4 * lane;
         for (int c = 0; c < 4; c++) out[c] = to_bf(__fdiv_rn(o[c], L));
