@@ -140,6 +140,43 @@ def test_chain_dependent_ops(dev):
     chain.destroy()
 
 
+def test_chain_sparse_segments(dev):
+    """Segments that few CTAs visit: a 32-row op (2 row blocks, so 2 CTAs)
+    between two large ones, a 4096-row op over K = 32 after it, and an op
+    that reads the first op's output two segments later (complete through
+    the waits of the segments between). Every waiting op bit-identical to the
+    single-op GEMV on the chain's own upstream output, twice in a row (the
+    segment counters are left zeroed for the next launch)."""
+    m = 3
+    specs = [(4096, 4096, None), (32, 4096, 0), (4096, 32, 1), (2048, 4096, 0), (17, 2048, 3)]  # (n, k, x from op)
+    x0h = synth.synth_x(m, 4096, 91)
+    x0 = to_dev_u16(x0h)
+    ws, ys, qs = [], [], []
+    for i, (n, k, _) in enumerate(specs):
+        q, s, _ = _op_inputs(n, k, 1, 970 + i)
+        qs.append((q, s))
+        ws.append(import_planes(dev, q, s))
+        ys.append(torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda"))
+    ops = []
+    for i, (w, y, (_, _, src)) in enumerate(zip(ws, ys, specs)):
+        xp = x0.data_ptr() if src is None else ys[src].data_ptr()
+        ops.append((w, xp, y.data_ptr(), m, 0, 0 if i == 0 else 1))
+    chain = hal.Chain(dev, ops)
+    for rep in range(2):
+        for y in ys:
+            y.fill_(float("nan"))
+        chain.run()
+        torch.cuda.synchronize()
+        rows = _oracle_rows(specs[0][0])
+        q, s = qs[0]
+        assert_parity(from_dev_bf16(ys[0])[:, rows], O.gemv_q(q[rows], s[rows], x0h), f"rep {rep} op 0")
+        for i in range(1, len(specs)):
+            ref = _raw(ws[i], ys[specs[i][2]], m, specs[i][0], False)
+            assert torch.equal(_bits(ys[i]), _bits(ref)), (rep, i)
+    assert dev.fault() == 0
+    chain.destroy()
+
+
 def test_chain_decode_set(dev):
     """Four layers of the 8B decode set (qkv, o, gateup, down) with fixed
     activations, every op after the previous (the decode step's order): the
