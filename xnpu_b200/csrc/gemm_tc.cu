@@ -195,7 +195,7 @@ __device__ __forceinline__ void store_out(void *y, int out_f32, size_t idx, floa
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, int n, int nb,
-            int kc_n, int m, int bn, int P, int D, int S, void *__restrict__ y, int out_f32)
+            int kc_n, int m, int bn, int P, int D, int S, int tile0, int tiles_n, void *__restrict__ y, int out_f32)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -215,7 +215,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
     float *part = reinterpret_cast<float *>(smem);  // split-K partial [bn][128] over the A/x rings
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tile_n = blockIdx.x, tile_m = blockIdx.y, z = blockIdx.z;
+    // output tile tile0 + blockIdx.x, feature tiles fastest (CTAs that run
+    // together share their x tiles in L2)
+    const int tile = tile0 + (int)blockIdx.x, tile_n = tile % tiles_n, tile_m = tile / tiles_n, z = blockIdx.z;
     const int rb0 = tile_n * kRb;
     const int m0 = tile_m * bn;
     const int kc_beg = (int)((long long)z * kc_n / S), kc_end = (int)((long long)(z + 1) * kc_n / S);
@@ -558,31 +560,46 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
     }
     const int tiles_n = (nb + kRb - 1) / kRb, tiles_m = (m + bn - 1) / bn;
     const long long tiles = (long long)tiles_n * tiles_m;
-    // split K over a cluster when the tiles leave CTA slots idle; at least 4
-    // chunks per slice
-    int S = 1;
+    if (tiles > (1ll << 30)) return cudaErrorInvalidValue;
     const long long slots = (long long)sm_count() * per_sm;
-    if (tiles < slots) {
-        S = (int)(slots / tiles);
-        if (S > kMaxSplit) S = kMaxSplit;
-        if (S > kc / 4) S = kc / 4;
-        if (S < 1) S = 1;
+    // Whole waves of tiles first; the tiles of a last, partial wave (or all
+    // of them when they leave CTA slots idle) in a second launch whose K is
+    // split over a cluster of S >= 2 CTAs per tile, at least 4 chunks per
+    // slice (a last wave of more than half the slots stays in the first).
+    // (Prefill 2048 x 4096 -> 14336: 896 tiles on 148 slots were 7 waves, the
+    // last of 8 tiles.)  The second launch's weight loads and prologue overlap
+    // the first one's tail (programmatic dependent launch).
+    long long full = tiles / slots * slots, rest = tiles - full;
+    if (rest * 2 > slots) {  // a last wave that cannot be split: one launch
+        full = tiles;
+        rest = 0;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(tiles_n, tiles_m, S);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = S;
-    cfg.attrs = attr;
-    cfg.numAttrs = S > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, D, S, y, out_f32);
+    const auto launch = [&](long long tile0, long long count, int S) -> cudaError_t {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)count, 1, S);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = S;
+        cfg.attrs = attr;
+        cfg.numAttrs = S > 1 ? 2 : 1;
+        return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, D, S, (int)tile0, tiles_n, y,
+                                  out_f32);
+    };
+    if (full > 0)
+        if (cudaError_t e = launch(0, full, 1); e != cudaSuccess) return e;
+    if (rest == 0) return cudaSuccess;
+    int S = (int)(slots / rest);
+    if (S > kMaxSplit) S = kMaxSplit;
+    if (S > kc / 4) S = kc / 4;
+    if (S < 1) S = 1;
+    return launch(full, rest, S);
 }
 
 unsigned int xq4_take_fault_gemm()
