@@ -44,6 +44,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <atomic>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -481,6 +482,267 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
                      : "memory");
 }
 
+// ------------------------------------------------------- persistent variant
+// Whole waves of tiles when one CTA fills an SM (BN > 64): each CTA walks the
+// tiles blockIdx.x, blockIdx.x + gridDim.x, ... of its launch.  The three
+// rings run on across tiles (the next tile's weights, x and A stream while the
+// current tile's last MMAs run), and the accumulator alternates between two
+// tensor-memory halves: four epilogue warps read out and store tile j while
+// the MMAs of tile j + 1 fill the other half.  Per tile this saves a CTA
+// launch, its prologue and an epilogue that nothing overlapped.
+constexpr int kEpiWarp0 = 11, kEpiWarps = 4;
+constexpr int kPtThreads = (kEpiWarp0 + kEpiWarps) * 32;
+
+__host__ __device__ constexpr size_t pt_smem_bytes(int bn, int P, int D)
+{
+    return 1024 + (size_t)D * kATileBytes + (size_t)D * x_tile_bytes(bn) + (size_t)P * kPackedBytes +
+           (size_t)(2 * P + 3 * D + 4) * 8 + 16;
+}
+
+__global__ void __launch_bounds__(kPtThreads, 1)
+gemm_pt_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap pmap, int n, int kc_n,
+               int m, int bn, int P, int D, int tile0, int count, int tiles_n, void *__restrict__ y, int out_f32)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const uint32_t xbytes = (uint32_t)x_tile_bytes(bn);
+    uint8_t *at = smem;                            // [D][128][64] bf16, swizzled
+    uint8_t *xt = at + (size_t)D * kATileBytes;     // [D][bn][64] bf16, swizzled
+    uint8_t *pk = xt + (size_t)D * xbytes;          // [P][8 row blocks][4 chunks]
+    uint64_t *pfull = reinterpret_cast<uint64_t *>(pk + (size_t)P * kPackedBytes);
+    uint64_t *pempty = pfull + P;
+    uint64_t *xfull = pempty + P;
+    uint64_t *afull = xfull + D;
+    uint64_t *sfree = afull + D;  // stage d's x and A slots free again (one MMA commit)
+    uint64_t *accf = sfree + D;   // [2] accumulator half complete
+    uint64_t *acce = accf + 2;    // [2] accumulator half read out
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntl = (count - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;  // this CTA's tiles
+    const int nk = kc_n;
+    const uint32_t acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+    const auto tile_of = [&](int j, int &rb0, int &m0) {
+        const int t = tile0 + (int)blockIdx.x + j * (int)gridDim.x;
+        rb0 = (t % tiles_n) * kRb;
+        m0 = (t / tiles_n) * bn;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P; s++) {
+            xq4d::mbar_init(&pfull[s], 1);
+            xq4d::mbar_init(&pempty[s], kDqWarps);
+        }
+        for (int s = 0; s < D; s++) {
+            xq4d::mbar_init(&xfull[s], 1);
+            xq4d::mbar_init(&sfree[s], 1);
+            xq4d::mbar_init(&afull[s], kDqWarps);
+        }
+        for (int h = 0; h < 2; h++) {
+            xq4d::mbar_init(&accf[h], 1);
+            xq4d::mbar_init(&acce[h], kEpiWarps);
+        }
+        xq4d::fence_barrier_init();
+    }
+    if (warp == kMmaWarp) {  // two accumulator halves
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         xq4d::smem_u32(tmem_slot)),
+                     "r"(2 * acc_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool failed = false;
+    xq4d::grid_dep_launch();  // as gemm_kernel: x and y wait for the previous launch below
+
+    if (warp == kPackWarp) {  // ------------------------------ packed-weight producer
+        if (lane == 0) {
+            const int npk = (nk + kPkChunks - 1) / kPkChunks;
+            int s = 0;
+            uint32_t ph = 0;
+            long long issued = 0;
+            for (int j = 0; j < ntl && !failed; j++) {
+                int rb0, m0;
+                tile_of(j, rb0, m0);
+                for (int i = 0; i < npk; i++) {
+                    if (issued >= P && !xq4d::mbar_wait(&pempty[s], ph ^ 1)) {
+                        failed = true;
+                        break;
+                    }
+                    xq4d::mbar_arrive_expect_tx(&pfull[s], kPackedBytes);
+                    tma_load_3d(pk + (size_t)s * kPackedBytes, &pmap, 0, i * kPkChunks, rb0, &pfull[s]);
+                    issued++;
+                    if (++s == P) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            // no copy may still be landing in shared memory when the CTA exits
+            for (long long q = issued > P ? issued - P : 0; q < issued; q++)
+                if (!xq4d::mbar_wait(&pfull[q % P], (uint32_t)(q / P) & 1)) failed = true;
+        }
+    } else if (warp == kXWarp) {  // ------------------------------ activation producer
+        if (lane == 0) {
+            xq4d::grid_dep_wait();
+            int s = 0;
+            uint32_t ph = 0;
+            long long issued = 0;
+            for (int j = 0; j < ntl && !failed; j++) {
+                int rb0, m0;
+                tile_of(j, rb0, m0);
+                for (int i = 0; i < nk; i++) {
+                    if (issued >= D && !xq4d::mbar_wait(&sfree[s], ph ^ 1)) {
+                        failed = true;
+                        break;
+                    }
+                    xq4d::mbar_arrive_expect_tx(&xfull[s], xbytes);
+                    tma_load_2d(xt + (size_t)s * xbytes, &xmap, i * kTileK, m0, &xfull[s]);
+                    issued++;
+                    if (++s == D) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            for (long long q = issued > D ? issued - D : 0; q < issued; q++)
+                if (!xq4d::mbar_wait(&xfull[q % D], (uint32_t)(q / D) & 1)) failed = true;
+        }
+    } else if (warp == kMmaWarp) {  // ------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16(kTileN, bn);
+            const uint32_t a_base = xq4d::smem_u32(at), x_base = xq4d::smem_u32(xt);
+            int sl = 0;
+            uint32_t ph = 0;
+            for (int j = 0; j < ntl && !failed; j++) {
+                const int h = j & 1;
+                // the epilogue has read this half's previous tile
+                if (j >= 2 && !xq4d::mbar_wait(&acce[h], (uint32_t)((j >> 1) - 1) & 1)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)h * acc_cols;
+                for (int i = 0; i < nk; i++) {
+                    if (!xq4d::mbar_wait(&xfull[sl], ph) || !xq4d::mbar_wait(&afull[sl], ph)) {
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t adesc = sw128_desc(a_base + (uint32_t)sl * kATileBytes);
+                    const uint64_t bdesc = sw128_desc(x_base + (uint32_t)sl * xbytes);
+#pragma unroll
+                    for (int kk = 0; kk < kTileK / 16; kk++)
+                        mma_bf16_ss(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (i | kk) != 0);
+                    mma_commit(&sfree[sl]);
+                    if (++sl == D) {
+                        sl = 0;
+                        ph ^= 1;
+                    }
+                }
+                mma_commit(&accf[h]);  // this tile's accumulator complete (or whatever was issued)
+            }
+        }
+    } else if (warp < kDqWarps) {  // ---------------------------- dequant (warp = row block)
+        const int g = lane >> 2, t = lane & 3;
+        const int gsel = g & 1;
+        int sp = 0, c = 0, sa = 0;
+        uint32_t pp = 0, pa = 0;
+        long long cnt = 0;
+        for (int j = 0; j < ntl && !failed; j++) {
+            for (int i = 0; i < nk && !failed; i++, cnt++) {
+                if (c == 0 && !xq4d::mbar_wait(&pfull[sp], pp)) {
+                    failed = true;
+                    break;
+                }
+                const uint8_t *up = pk + (size_t)sp * kPackedBytes + (warp * kPkChunks + c) * XQ4G_UNIT_BYTES;
+                const uint4 cw = *reinterpret_cast<const uint4 *>(up + lane * 16);
+                const uint2 sw = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+                __syncwarp();
+                // a tile's packed stages hold 4 chunks each, the last one
+                // whatever remains of K
+                if (c == kPkChunks - 1 || i == nk - 1) {
+                    if (lane == 0) xq4d::mbar_arrive(&pempty[sp]);
+                    c = 0;
+                    if (++sp == P) {
+                        sp = 0;
+                        pp ^= 1;
+                    }
+                } else {
+                    c++;
+                }
+                if (cnt >= D && !xq4d::mbar_wait(&sfree[sa], pa ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
+                uint4 lo[2], hi[2];
+#pragma unroll
+                for (int G = 0; G < 2; G++) {
+                    const uint32_t sg = G ? sw.y : sw.x;
+                    const uint32_t s_lo = __byte_perm(sg, 0, 0x1010), s_hi = __byte_perm(sg, 0, 0x3232);
+                    uint32_t a0[4], a1[4];
+                    xq4d::dequant_word(words[2 * G], s_lo, s_hi, a0);
+                    xq4d::dequant_word(words[2 * G + 1], s_lo, s_hi, a1);
+                    lo[G] = make_uint4(a0[0], a0[2], a1[0], a1[2]);
+                    hi[G] = make_uint4(a0[1], a0[3], a1[1], a1[3]);
+                }
+                uint8_t *a = at + (size_t)sa * kATileBytes;
+                const int r0 = warp * XQ4G_ROWS + g;
+                *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * gsel + t)) = gsel ? lo[1] : lo[0];
+                *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * (1 - gsel) + t)) = gsel ? lo[0] : lo[1];
+                *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * gsel + t)) = gsel ? hi[1] : hi[0];
+                *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * (1 - gsel) + t)) = gsel ? hi[0] : hi[1];
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) xq4d::mbar_arrive(&afull[sa]);
+                if (++sa == D) {
+                    sa = 0;
+                    pa ^= 1;
+                }
+            }
+        }
+    } else {  // ------------------------------------------------ epilogue warps
+        // warp w reads TMEM lanes 32 * (w % 4).. (the tile's features), every column
+        xq4d::grid_dep_wait();  // y may be read by the previous launch
+        const int q4 = warp & 3, f = q4 * 32 + lane;
+        for (int j = 0; j < ntl; j++) {
+            const int h = j & 1;
+            if (!xq4d::mbar_wait(&accf[h], (uint32_t)(j >> 1) & 1)) failed = true;
+            tc_fence_after();
+            int rb0, m0;
+            tile_of(j, rb0, m0);
+            const int feat = rb0 * XQ4G_ROWS + f;
+            for (int c0 = 0; c0 < bn; c0 += 8) {
+                uint32_t r[8];
+                tmem_ld8(tmem + (uint32_t)h * acc_cols + ((uint32_t)(q4 * 32) << 16) + (uint32_t)c0, r);
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const int tok = m0 + c0 + c;
+                    if (!failed && tok < m && feat < n) store_out(y, out_f32, (size_t)tok * n + feat, __uint_as_float(r[c]));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) xq4d::mbar_arrive(&acce[h]);  // the MMAs may refill this half
+        }
+    }
+    if (failed) atomicOr(&g_xq4_fault, XQ4_FAULT_GEMM_WAIT);
+    // no MMA may still be writing the accumulator when it is freed: the MMA
+    // thread waits for its last commit of each half (bounded)
+    if (warp == kMmaWarp && lane == 0)
+        for (int j = ntl > 2 ? ntl - 2 : 0; j < ntl; j++) xq4d::mbar_wait(&accf[j & 1], (uint32_t)(j >> 1) & 1);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * acc_cols)
+                     : "memory");
+}
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 {
@@ -555,6 +817,8 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
         cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gemm_pt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
@@ -592,8 +856,29 @@ cudaError_t xq4_launch_gemm(const uint8_t *pack, int n, int k, const void *x, in
         return cudaLaunchKernelEx(&cfg, gemm_kernel, xmap, pmap, n, nb, kc, m, bn, P, D, S, (int)tile0, tiles_n, y,
                                   out_f32);
     };
-    if (full > 0)
+    // one CTA fills an SM and every CTA has two tiles or more: the persistent
+    // kernel walks the whole waves (with one tile per CTA it has nothing to
+    // overlap, and its four epilogue warps drain a tile slower than eight)
+    if (full >= 2 * slots && per_sm == 1) {
+        const size_t pt_smem = pt_smem_bytes(bn, P, D);
+        if (pt_smem > (size_t)kMaxSmem) return cudaErrorInvalidValue;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)std::min(full, slots));
+        cfg.blockDim = dim3(kPtThreads);
+        cfg.dynamicSmemBytes = pt_smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pt_kernel, xmap, pmap, n, kc, m, bn, P, D, 0, (int)full,
+                                               tiles_n, y, out_f32);
+            e != cudaSuccess)
+            return e;
+    } else if (full > 0) {
         if (cudaError_t e = launch(0, full, 1); e != cudaSuccess) return e;
+    }
     if (rest == 0) return cudaSuccess;
     int S = (int)(slots / rest);
     if (S > kMaxSplit) S = kMaxSplit;
