@@ -256,7 +256,8 @@ int xq4_chain_run(const xq4_chain *chain, void *stream);
  * (ert.rs:147-151): XQ4_OK when the op at `seq` and everything queued before
  * it has completed, XQ4_ETIMEDOUT if timeout_ns elapsed first (the work stays
  * queued and a later wait may succeed), XQ4_ECUDA if the device reported an
- * error. */
+ * error.  The calling thread polls without sleeping for the first 2 ms, then
+ * sleeps 20 us between polls. */
 int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns);
 /* Timeline point of the newest submitted op. */
 uint64_t xq4_last_seq(const xq4_device *dev);

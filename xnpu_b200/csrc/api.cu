@@ -724,8 +724,10 @@ extern "C" int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns)
     uint64_t probe = seq;
     if (dev->last_seq >= (uint64_t)kRing && seq <= dev->last_seq - kRing) probe = dev->last_seq - kRing + 1;
     cudaEvent_t ev = dev->ring[probe % kRing];
+    // Poll without sleeping for the first 2 ms (a decode step or a chain is
+    // shorter: a sleep's timer slack would add tens of microseconds to every
+    // wait), then sleep 20 us between polls.
     const uint64_t t0 = now_ns();
-    unsigned spins = 0;
     for (;;) {
         cudaError_t e = cudaEventQuery(ev);
         if (e == cudaSuccess) {
@@ -733,10 +735,11 @@ extern "C" int xq4_wait(xq4_device *dev, uint64_t seq, int64_t timeout_ns)
             return XQ4_OK;
         }
         if (e != cudaErrorNotReady) return cuda_fail(e, "timeline wait");
-        if (timeout_ns >= 0 && (int64_t)(now_ns() - t0) >= timeout_ns)
+        const int64_t waited = (int64_t)(now_ns() - t0);
+        if (timeout_ns >= 0 && waited >= timeout_ns)
             return xq4_fail(XQ4_ETIMEDOUT, "seq %llu not complete after %lld ns", (unsigned long long)seq,
                             (long long)timeout_ns);
-        if (++spins > 64) usleep(20);
+        if (waited > 2000000) usleep(20);
     }
 }
 
