@@ -51,7 +51,7 @@ constexpr int kMaxGroup = 8;      // q heads per kv head
 constexpr int kMaxSpan = 384;     // positions per CTA (its K and V rows and scores in shared memory)
 constexpr int kMaxSplits = 64;    // splits per kv head (the merge covers them in two lane rounds)
 #ifndef XQ4_ATTN_MIN_SPAN
-#define XQ4_ATTN_MIN_SPAN 64
+#define XQ4_ATTN_MIN_SPAN 32
 #endif
 constexpr int kMinSpan = XQ4_ATTN_MIN_SPAN;  // positions a split takes before the token uses another split (measured)
 // One split's partial of one head in the workspace: max, sum, two pad words
