@@ -316,24 +316,24 @@ __device__ __forceinline__ bool p2p_usable(const xq4_p2p_poison &p, int rank, in
     return v == 0u;
 }
 
-// Copy the peers' words i = lane, lane + 32, ... < total_w of an inbox
+// Copy the peers' words i = tid, tid + nthr, ... < total_w of an inbox
 // (value bits | epoch << 32) into y (bf16 or f32 values) once each carries
 // epoch e; idx_of(i) gives word i's index in the inbox half and in y (the same
-// [tok][n_total] position; below XQ4_FUSED_MAX_VALUES).  Eight loads per lane
-// are in flight together: one at a time, the loop cost a round trip to
-// memory per 32 words.  False when a word is still stale after the bounded
-// wait (2 s from t0).
+// [tok][n_total] position; below XQ4_FUSED_MAX_VALUES).  Eight loads per
+// thread are in flight together: one at a time, the loop cost a round trip
+// to memory per nthr words.  False when a word is still stale after the
+// bounded wait (2 s from t0).
 template <class IdxF>
-__device__ __forceinline__ bool gather_inbox(const unsigned long long *in, unsigned e, int total_w, int lane,
-                                             uint64_t t0, bool out_f32, void *y, IdxF idx_of)
+__device__ __forceinline__ bool gather_inbox(const unsigned long long *in, unsigned e, int total_w, int tid,
+                                             int nthr, uint64_t t0, bool out_f32, void *y, IdxF idx_of)
 {
     constexpr int kBatch = 8;
-    for (int i0 = lane; i0 < total_w; i0 += 32 * kBatch) {
+    for (int i0 = tid; i0 < total_w; i0 += nthr * kBatch) {
         int idx[kBatch];
         unsigned long long w[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; j++) {
-            const int i = i0 + 32 * j;
+            const int i = i0 + nthr * j;
             idx[j] = i < total_w ? idx_of(i) : -1;
             w[j] = idx[j] >= 0 ? xq4d::ld_sys_u64(in + idx[j]) : 0ull;
         }
@@ -492,7 +492,7 @@ gemv_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n,
             const int per_peer = m * span, total_w = (p2p.nranks - 1) * per_peer;
             const uint64_t t0 = xq4d::global_ns();
             if (alive && xchg &&
-                !gather_inbox(in, e, total_w, lane, t0, out_f32 != 0, y, [&](int i) {
+                !gather_inbox(in, e, total_w, lane, 32, t0, out_f32 != 0, y, [&](int i) {
                     const int qi = i / per_peer, rem = i - qi * per_peer;
                     const int tok = rem / span, row = r0 + (rem - tok * span);
                     const int q = qi < p2p.rank ? qi : qi + 1;
@@ -946,6 +946,43 @@ __device__ __forceinline__ bool consume_stage_w4a8(uint32_t stage, uint64_t *ful
     return true;
 }
 
+// The peers' rows of this CTA's ranges of the sharded ops among its visits
+// [vf, vl] go from the inbox into y, threads tid = 0..nthr-1 sharing the
+// words.  Each peer's CTA with this index computed them (equal shards, equal
+// chains), and every CTA sends its words before it waits, so no wait depends
+// on a waiting CTA.  A word still stale after the bounded wait raises fault
+// bit 0x8 and poisons the communicator.
+__device__ __forceinline__ void chain_gather(const xq4_chain_op_dev *__restrict__ ops, const xq4_chain_plan &plan,
+                                             const xq4_chain_p2p &p2p, int vf, int vl, unsigned e, size_t half,
+                                             int tid, int nthr)
+{
+    const uint64_t t0 = xq4d::global_ns();
+    for (int s = vf; s <= vl; s++) {
+        const int4 si = __ldg(plan.visits + s);
+        const xq4_chain_op_dev so = ops[si.x];
+        if (!so.shard) continue;
+        // this CTA's output rows of the op (row pairs for SwiGLU; row blocks
+        // hold 16 rows, so a range never splits a pair)
+        const int sh = so.swiglu ? 1 : 0;
+        const int r0 = (si.y * XQ4G_ROWS) >> sh, span = (min(si.z * XQ4G_ROWS, so.n) >> sh) - r0;
+        if (span <= 0) continue;
+        const int ns = so.n >> sh;
+        const size_t stride = (size_t)so.n_total >> sh;
+        const unsigned long long *in = p2p.inbox[p2p.rank] + half + so.inbox_off;
+        const int per_peer = so.m * span, total_w = (p2p.nranks - 1) * per_peer;
+        if (!gather_inbox(in, e, total_w, tid, nthr, t0, so.out_f32 != 0, so.y, [&](int i) {
+                const int qi = i / per_peer, rem = i - qi * per_peer;
+                const int tok = rem / span, row = r0 + (rem - tok * span);
+                const int q = qi < p2p.rank ? qi : qi + 1;
+                return (int)(tok * stride) + q * ns + row;
+            })) {
+            atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
+            p2p_poison(p2p.poison, p2p.nranks);
+            return;
+        }
+    }
+}
+
 // W8: the chain holds W4A8 ops.  The W4A8 path is compiled only into that
 // instantiation: inside the register-capped fp16 kernel it cost the fp16 ops
 // 6 % (measured on B200, the 32-layer decode set).
@@ -1145,40 +1182,12 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
                 }
             }
             if (!(vi.w & kVisitLast)) continue;
-            // The CTA's last visit in its segment: the peers' rows of its
-            // ranges of the segment's sharded ops go from the inbox into y.
-            // Each peer's CTA with this index computed them (equal shards,
-            // equal chains), and every CTA sends its words before it waits,
-            // so no wait depends on a waiting CTA.
-            if (xchg) {
-                const uint64_t t0 = xq4d::global_ns();
-                bool ok = alive;
-                for (int s = pend; ok && s <= v; s++) {
-                    const int4 si = __ldg(plan.visits + s);
-                    const xq4_chain_op_dev so = ops[si.x];
-                    if (!so.shard) continue;
-                    const int s0 = si.y, s1 = si.z;
-                    // this CTA's output rows of the op (row pairs for SwiGLU;
-                    // row blocks hold 16 rows, so a range never splits a pair)
-                    const int sh = so.swiglu ? 1 : 0;
-                    const int r0 = (s0 * XQ4G_ROWS) >> sh, span = (min(s1 * XQ4G_ROWS, so.n) >> sh) - r0;
-                    if (span <= 0) continue;
-                    const int ns = so.n >> sh;
-                    const size_t stride = (size_t)so.n_total >> sh;
-                    const unsigned long long *in = p2p.inbox[p2p.rank] + half + so.inbox_off;
-                    const int per_peer = so.m * span, total_w = (p2p.nranks - 1) * per_peer;
-                    ok = gather_inbox(in, e, total_w, lane, t0, so.out_f32 != 0, so.y, [&](int i) {
-                        const int qi = i / per_peer, rem = i - qi * per_peer;
-                        const int tok = rem / span, row = r0 + (rem - tok * span);
-                        const int q = qi < p2p.rank ? qi : qi + 1;
-                        return (int)(tok * stride) + q * ns + row;
-                    });
-                    if (!ok) {
-                        atomicOr(&g_xq4_fault, XQ4_FAULT_PEER_WAIT);
-                        p2p_poison(p2p.poison, p2p.nranks);
-                    }
-                }
-            }
+            // The CTA's last visit in its segment: before a later segment may
+            // read them, the peers' rows of its ranges of the segment's
+            // sharded ops go from the inbox into y (the last segment's
+            // rows are copied by the consumer warps, after their last stage).
+            if (xchg && alive && seg + 1 < plan.n_seg)
+                chain_gather(ops, plan, p2p, pend, v, e, half, lane, 32);
             pend = v + 1;
             // this CTA's rows of the segment are written (the warp barrier
             // orders every lane's stores before lane 0's release); no
@@ -1197,6 +1206,9 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
 
     // ------------------------------------------------------------ consumers
     xq4d::grid_dep_wait();
+    // this launch's inbox epoch, read before this CTA's reducer can count
+    // out (after which the last CTA out advances it)
+    const unsigned ep = p2p.nranks > 1 ? *reinterpret_cast<volatile const unsigned *>(p2p.epoch) + 1u : 0u;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t ring_s = xq4d::smem_u32(ring);
     const uint32_t xs[1] = {0u};
@@ -1299,6 +1311,16 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
                 return;
             }
         }
+    }
+    // the last segment's copy-in of the peers' rows, shared by the consumer
+    // warps (one warp walking it alone cost tens of microseconds of the
+    // launch's tail at 8 ranks)
+    if (p2p.nranks > 1 && v1 > v0) {
+        int vf = v1;
+        while (vf > v0 && (__ldg(plan.visits + vf - 1).w >> 2) == plan.n_seg - 1) vf--;
+        if (vf < v1 && p2p_usable(p2p.poison, p2p.rank, lane))
+            chain_gather(ops, plan, p2p, vf, v1 - 1, ep, (size_t)(ep & 1u) * p2p.half_words,
+                         warp * 32 + lane, kConsumerThreads);
     }
 }
 
