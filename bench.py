@@ -98,6 +98,7 @@ class ClockSampler:
         self.rows = []
         self.err = None
         self._stop = threading.Event()
+        self._ready = threading.Event()
 
     def _poll(self):
         try:
@@ -109,14 +110,19 @@ class ClockSampler:
                 mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
                 bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
                 self.rows.append((mhz, bits))
+                self._ready.set()
                 time.sleep(0.002)
         except Exception as e:  # NVML missing: report it, do not fail the bench
             self.err = f"{type(e).__name__}: {e}"
+        finally:
+            self._ready.set()
 
     def __enter__(self):
+        # NVML's initialisation (~0.1 s) finishes before the timed region:
+        # inside it, it held up the launching thread between the events
         self._t = threading.Thread(target=self._poll, daemon=True)
         self._t.start()
-        time.sleep(0.01)
+        self._ready.wait(10.0)
         return self
 
     def __exit__(self, *exc):
