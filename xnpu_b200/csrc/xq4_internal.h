@@ -166,10 +166,9 @@ static inline bool xq4_use_gemv(int m) { return m < XQ4_GEMM_MIN_M; }
 cudaError_t xq4_launch_gemv(const uint8_t *pack, int n, int k, const void *x, int m, void *y,
                             int out_f32, cudaStream_t st,
                             const struct xq4_p2p_out *p2p = nullptr);
-// One persistent launch over a chain of GEMVs (m <= 8 each); `done` holds
-// n_ops + 1 zeroed counters (left zeroed at the end of the launch).
-// `rng` holds each op's row-block range per CTA ([op][cta], grid CTAs;
-// xq4_chain_ranges), built for `grid` = xq4_gemv_chain_grid() at create.
+// One persistent launch over a chain of GEMVs (m <= 8 each) by the plan
+// (per-CTA visit lists and segment counters, the counters left zeroed at the
+// end of the launch), built for `grid` = xq4_gemv_chain_grid() at create.
 // has_w4a8: the chain holds W4A8 ops (the kernel instantiation with that path).
 cudaError_t xq4_launch_gemv_chain(const struct xq4_chain_op_dev *ops, const struct xq4_chain_plan &plan, int grid,
                                   const struct xq4_chain_prep_dev *preps, int n_preps,
