@@ -913,26 +913,42 @@ __device__ __forceinline__ bool consume_stage_w4a8(uint32_t stage, uint64_t *ful
                                                    float (&acc)[4])
 {
     const int g = lane >> 2, t = lane & 3;
-    if (!xq4d::mbar_wait(full, phase)) return false;
+    // two chunks at a time: their int8 activations and group entries (the
+    // prep's output, L2-resident) are loaded before the stage wait and
+    // before the chunks' code words, so the loads' latency overlaps it
+    constexpr int R = 2;
 #pragma unroll
-    for (int c = 0; c < kCpw; c++) {
-        const int cl = warp + c * kConsumerWarps;  // chunk within the stage
-        const int kc = kc0 + cl;
-        if (kc < kc_n) {
+    for (int c0 = 0; c0 < kCpw; c0 += R) {
+        uint2 bx[R][2];
+        uint4 ex[R][2];  // {cx(2t), d(2t), cx(2t+1), d(2t+1)}
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const int kc = kc0 + warp + (c0 + c) * kConsumerWarps;
+#pragma unroll
+            for (int G2 = 0; G2 < 2; G2++) {
+                const int grp = kc * 2 + G2;
+                bx[c][G2] = kc < kc_n ? xq4d::ldg_v2(xrow + grp * 32 + 8 * t) : make_uint2(0, 0);
+                ex[c][G2] = kc < kc_n ? xq4d::ldg_v4(qtbl + grp * 8 + 2 * t) : make_uint4(0, 0, 0, 0);
+            }
+        }
+        if (c0 == 0 && !xq4d::mbar_wait(full, phase)) return false;
+#pragma unroll
+        for (int c = 0; c < R; c++) {
+            const int cl = warp + (c0 + c) * kConsumerWarps;  // chunk within the stage
+            if (kc0 + cl >= kc_n) continue;
             const uint32_t up = stage + cl * XQ4G_UNIT_BYTES;
             const uint4 cw = xq4d::lds_v4(up + lane * 16);
             const uint2 sw = xq4d::lds_v2(up + XQ4G_CODE_BYTES + g * 8);
             const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
             for (int G2 = 0; G2 < 2; G2++) {
-                const int grp = kc * 2 + G2;
-                const uint2 b = xq4d::ldg_v2(xrow + grp * 32 + 8 * t);
-                const uint4 e = xq4d::ldg_v4(qtbl + grp * 8 + 2 * t);  // {cx(2t), d(2t), cx(2t+1), d(2t+1)}
+                const uint2 bb = bx[c][G2];
+                const uint4 e = ex[c][G2];
                 const uint32_t w0 = words[2 * G2], w1 = words[2 * G2 + 1];
                 const uint32_t a[4] = {w0 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu,
                                        (w1 >> 4) & 0x0F0F0F0Fu};
                 int T[4];
-                xq4d::mma_u8s8_16832(T, a, b.x, b.y, (int)e.x, (int)e.z);
+                xq4d::mma_u8s8_16832(T, a, bb.x, bb.y, (int)e.x, (int)e.z);
                 const uint32_t sg = G2 ? sw.y : sw.x;
                 const float s_lo = __uint_as_float(sg << 16), s_hi = __uint_as_float(sg & 0xFFFF0000u);
                 const float d0 = __uint_as_float(e.y), d1 = __uint_as_float(e.w);
