@@ -439,6 +439,7 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         d.spr = (d.kc + XQ4_GEMV_STAGE_CHUNKS_ABI - 1) / XQ4_GEMV_STAGE_CHUNKS_ABI;
         d.shard = o.comm && p2p.nranks > 1;
         d.residual = (const uint16_t *)o.residual_dev;
+        d.res_ext = 0;
         d.swiglu = o.swiglu != 0;
         if (o.residual_dev || o.swiglu || o.norm_w_dev) {
             if (o.comm && o.residual_dev) return xq4_fail(XQ4_EINVAL, "op %d: a residual epilogue on a sharded op", i);
@@ -497,6 +498,18 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
     const size_t tab_bytes = align(tab.size() * sizeof(xq4_chain_op_dev));
     const size_t done_bytes = align(((size_t)n_seg + 1) * sizeof(unsigned));
     size_t img_bytes = 0;
+    // residuals no op of the chain writes (the reducer reads those before the
+    // consumers hand over the row block)
+    for (int i = 0; i < n_ops; i++) {
+        if (!ops[i].residual_dev) continue;
+        const char *r0 = (const char *)ops[i].residual_dev, *r1 = r0 + (size_t)ops[i].m * ops[i].w->n * 2;
+        bool written = false;
+        for (int j = 0; j < n_ops && !written; j++) {
+            const char *y0 = (const char *)ops[j].y_dev;
+            written = r0 < y0 + y_bytes(j) && y0 < r1;
+        }
+        tab[(size_t)i].res_ext = written ? 0 : 1;
+    }
     for (int i = 0; i < n_ops; i++) {
         const xq4_chain_op &o = ops[i];
         const char *x0 = (const char *)o.x_dev, *x1 = x0 + (size_t)o.m * o.w->k * 2;

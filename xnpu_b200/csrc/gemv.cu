@@ -1107,6 +1107,18 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
                 // bf16 and the partials added in f32 in chunk order, as
                 // w4a8_kernel (the reference's w4u_read_c, main.rs:3066-3091)
                 float val[4] = {0.f, 0.f, 0.f, 0.f};
+                // a residual no op of this chain writes: loaded before the
+                // consumers hand over the row block
+                float resv[4] = {0.f, 0.f, 0.f, 0.f};
+                if (op.residual && op.res_ext) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int oo = 32 * j + lane, row = rb * XQ4G_ROWS + (oo & 15);
+                        if (oo < op.m * 16 && row < op.n)
+                            resv[j] = __uint_as_float((uint32_t)xq4d::ldcg_u16(op.residual + (size_t)(oo >> 4) * op.n + row)
+                                                      << 16);
+                    }
+                }
                 const int nst = (W8 && op.w4a8) ? op.spr : 1;
                 for (int st = 0; st < nst; st++, rbl++) {
                     const int buf = rbl % kRedBufs;
@@ -1174,7 +1186,8 @@ gemv_chain_kernel(const xq4_chain_op_dev *__restrict__ ops, const __grid_constan
                     if (op.residual) {  // add_bf16 (main.rs:4726-4730) of the op's bf16 output
                         const size_t ri = (size_t)tok * op.n + row;
                         const float hb = __bfloat162float(__float2bfloat16_rn(sum));
-                        const float res = __uint_as_float((uint32_t)xq4d::ldcg_u16(op.residual + ri) << 16);
+                        const float res = op.res_ext ? resv[j]
+                                                     : __uint_as_float((uint32_t)xq4d::ldcg_u16(op.residual + ri) << 16);
                         reinterpret_cast<__nv_bfloat16 *>(op.y)[ri] = __float2bfloat16_rn(__fadd_rn(hb, res));
                         continue;
                     }

@@ -85,6 +85,7 @@ struct xq4_chain_op_dev {
     // the row pairs (2i, 2i+1) into y[tok][n/2] (sharded: y[tok][n_total/2],
     // this rank's pairs from row_off/2).
     const uint16_t *residual;
+    int res_ext;          // no op of the chain writes the residual: the reducer may read it early
     int swiglu;
     // W4A8 (the reference's NPU numerics): x quantized by the prep to int8
     // per 32-K group; per group one integer MMA, times s_w * d_x; each stage
