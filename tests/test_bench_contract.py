@@ -26,3 +26,18 @@ def test_reference_arm_line():
     assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["sample"] and cb["value"] == d["value"]
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_clock_sampler_ready_before_the_timed_region():
+    """The NVML sampler has finished starting (or failed to: no NVML here)
+    when its context opens, so its initialisation is never inside the timed
+    region; without NVML it reports why instead of failing the bench."""
+    import time
+    sys.path.insert(0, str(ROOT))
+    import bench
+    t0 = time.time()
+    with bench.ClockSampler(0) as clk:
+        assert clk._ready.is_set()
+    assert time.time() - t0 < 10.0
+    s = clk.summary()
+    assert set(s) >= {"sm_mhz", "sm_max_mhz", "reasons"}
