@@ -8,7 +8,9 @@
 #include <string.h>
 #include <time.h>
 #include <unistd.h>
+#include <map>
 #include <new>
+#include <tuple>
 #include <vector>
 
 #include "xq4_internal.h"
@@ -510,9 +512,25 @@ extern "C" int xq4_chain_create(xq4_device *dev, const xq4_chain_op *ops, int n_
         }
         tab[(size_t)i].res_ext = written ? 0 : 1;
     }
+    // An activation whose readers (ops without RMSNorm or W4A8) stream fewer
+    // chunks in all than the single-op GEMV's fp16 threshold keeps the bf16
+    // path: its prep launch would cost more than the fp16 path saves
+    // (measured: the decode step's o chain, 7.7 -> 6.4 us per layer), and the
+    // ops then compute along the same path as the single-op GEMV.
+    // A sharded op counts at its full size, so that every rank and the
+    // unsharded op take the same path.
+    std::map<std::tuple<const void *, int, int>, long long> x_chunks;
+    for (int i = 0; i < n_ops; i++)
+        if (!ops[i].norm_w_dev && !ops[i].w4a8) {
+            const xq4_chain_op_dev &d = tab[(size_t)i];
+            const long long rbs = d.shard ? (d.n_total + XQ4G_ROWS - 1) / XQ4G_ROWS : d.nb;
+            x_chunks[std::make_tuple(ops[i].x_dev, ops[i].m, ops[i].w->k)] += rbs * d.kc;
+        }
     for (int i = 0; i < n_ops; i++) {
         const xq4_chain_op &o = ops[i];
         const char *x0 = (const char *)o.x_dev, *x1 = x0 + (size_t)o.m * o.w->k * 2;
+        if (!o.norm_w_dev && !o.w4a8 && x_chunks[std::make_tuple(o.x_dev, o.m, o.w->k)] < XQ4_XH_MIN_CHUNKS)
+            continue;  // bf16 path
         bool written = false;
         for (int j = 0; j < n_ops && !written; j++) {
             const char *y0 = (const char *)ops[j].y_dev;

@@ -108,7 +108,7 @@ constexpr int kXhMaxElems = 20480;
 // on the critical path; it pays for itself only on large matrices (measured
 // on B200 at m = 1: 28672 x 4096 and 128256 x 4096 are faster with it,
 // 14336 x 4096, 6144 x 4096, 4096 x 4096 and 4096 x 14336 without).
-constexpr long long kXhMinChunks = 98304;
+constexpr long long kXhMinChunks = XQ4_XH_MIN_CHUNKS;
 constexpr int kXhMaxBytes = 46080;
 __host__ __device__ constexpr bool xh_fits(int m, int kp)
 {

@@ -157,6 +157,10 @@ struct xq4_weight {
 // 16-token launches) streams the weights.  Measured on B200 (gate
 // 14336x4096): GEMV 19 us at m = 16 and 29 us at m = 24 against the GEMM's
 // 33 and 35 us; equal near m = 28; the GEMM is ahead from m = 32.
+// Chunks (16 rows x 64 K) from which the fp16 activation path pays for its
+// prologue (the single-op GEMV's staging, the chain's prep launch); below it
+// both run the bf16 path.
+#define XQ4_XH_MIN_CHUNKS 98304LL
 #ifndef XQ4_GEMM_MIN_M
 #define XQ4_GEMM_MIN_M 25
 #endif
