@@ -696,7 +696,7 @@ def decode_step_run(dev, weights, comm, world, stream, timed, args, peak, pos=10
     base 500000, random-init RMSNorm weights), one token at context position
     `pos` over 4096-position KV caches: per layer RMSNorm + qkv, RoPE +
     KV-cache append + GQA attention, o + residual, RMSNorm + gate/up + SwiGLU
-    (column-sharded at N > 1) + down + residual (xnpu_b200.decode, 7 launches
+    (column-sharded at N > 1) + down + residual (xnpu_b200.decode, 6 launches
     per layer), captured once in a CUDA graph and replayed."""
     import torch
     from xnpu_b200 import decode, synth

@@ -12,7 +12,8 @@ Per layer, as the reference orders it:
     xn = rms_norm(x, ln2)                       main.rs:8326
     x = x + W_down swiglu(W_gateup xn)          main.rs:8327-8337
 
-runs as three GEMV chains and one attention launch:
+runs as three GEMV chains and one attention launch (six launches with the
+8B shapes: chains 1 and 3 launch a prep kernel for their RMSNorm first):
 
   * chain 1: qkv, with the RMSNorm fused into the chain's activation prep;
   * attention: RoPE, q/k norm, KV-cache append and attention (xq4_attn_decode);
@@ -28,6 +29,10 @@ There is no host fallback: every launch goes through libxq4.
 import numpy as np
 
 from . import hal, synth
+
+# The library's fp16-path threshold (XQ4_XH_MIN_CHUNKS, 16-row x 64-K chunks):
+# a chain activation whose readers stream fewer chunks gets no prep launch.
+XH_MIN_CHUNKS = 98304
 
 
 class DecodeLayerWeights:
@@ -81,7 +86,12 @@ class DecodeStep:
                                   {"norm_w": p(lw.ln2), "eps": eps, "swiglu": True}),
                                  (lw.down, p(self.inter), p(self.x), 1, 0, 1, None, {"residual": p(self.h1)})])
             self.chains.append((c1, c2, c3))
-        self.launches_per_step = 7 * len(layers)  # 3 chains (+ a prep each) and the attention kernel
+        # per layer: chains 1 and 3 (each with its prep, their RMSNorm), the
+        # attention kernel, chain 2 (its prep only when the o projection streams
+        # at least XH_MIN_CHUNKS chunks: below that the library keeps the bf16
+        # path and launches no prep)
+        o_chunks = (hidden + 15) // 16 * ((heads * 128 + 63) // 64)
+        self.launches_per_step = (5 + (2 if o_chunks >= XH_MIN_CHUNKS else 1)) * len(layers)
 
     def run(self, stream=None):
         """One token through every layer: x (the residual stream) in, x out;
