@@ -321,9 +321,11 @@ def main():
     ap.add_argument("--skip-lmhead", action="store_true", help="profiler captures only")
     ap.add_argument("--skip-configs", action="store_true",
                     help="profiler captures only: no config 0/2/3 objects, no W4A8 or other step forms")
-    ap.add_argument("--kernel-case", choices=["gemv", "gemm", "w4a8"],
+    ap.add_argument("--kernel-case", choices=["gemv", "gemm", "w4a8", "attn"],
                     help="profiler captures: one projection launched warmup+steps times on GPU 0 "
-                         "(gemv and w4a8: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048)")
+                         "(gemv and w4a8: 65536x4096 at m=1, 151 MB of weights; gemm: 14336x4096 at m=2048; "
+                         "attn: decode attention, 32 q over 8 kv heads, 4096-position caches, position "
+                         "--case-m or 1024)")
     ap.add_argument("--case-m", type=int, default=None, help="token count of --kernel-case")
     ap.add_argument("--case-n", type=int, default=None, help="rows of --kernel-case")
     ap.add_argument("--case-k", type=int, default=None, help="K of --kernel-case")
@@ -902,12 +904,49 @@ def lmhead_run(dev, rank, world, comm, L, stream, timed, reps=20):
             "logits_gather_bytes_in": (n - (r1 - r0)) * 4, "parity_rank0": parity}
 
 
+def attn_case(args):
+    """Decode attention of the 8B shapes (32 q heads over 8 kv heads, head
+    dim 128, RoPE base 500000, 4096-position caches) at one position,
+    launched warmup+steps times (the profiler captures' command)."""
+    import torch
+    from xnpu_b200 import hal
+    dev = hal.Device.open(0)
+    heads, nkv, cs = 32, 8, 4096
+    pos = args.case_m if args.case_m is not None else 1024
+    g = torch.Generator(device="cuda").manual_seed(5)
+    qkv = torch.randn((heads + 2 * nkv) * 128, device="cuda", generator=g).to(torch.bfloat16)
+    kc = torch.randn((nkv, cs, 128), device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn((nkv, cs, 128), device="cuda", generator=g).to(torch.bfloat16)
+    pd = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    out = torch.empty(heads * 128, dtype=torch.bfloat16, device="cuda")
+    at = hal.Attention(dev, heads, nkv, cs, 500000.0)
+    stream = torch.cuda.Stream()
+    for _ in range(args.warmup):
+        at.decode(qkv, kc, vc, pd, out=out, stream=stream)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        at.decode(qkv, kc, vc, pd, out=out, stream=stream)
+    b.record(stream)
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / max(1, args.steps)
+    kv_bytes = 2 * nkv * (pos + 1) * 128 * 2
+    print(json.dumps({"kernel_case": "attn", "heads": heads, "nkv": nkv, "pos": pos, "us_per_launch": us,
+                      "kv_gbs": kv_bytes / us / 1e3, "fault": dev.fault()}), flush=True)
+    at.destroy()
+    dev.close()
+
+
 def kernel_case(args):
     """One projection launched warmup+steps times through the C ABI (the
     small, single-kernel command that profiler captures run on)."""
     import torch
     from xnpu_b200 import hal, lib, synth
     from xnpu_b200._lib import check
+    if args.kernel_case == "attn":
+        attn_case(args)
+        return
     n, k, m = (14336, 4096, 2048) if args.kernel_case == "gemm" else (65536, 4096, 1)
     m = args.case_m or m
     n = args.case_n or n
