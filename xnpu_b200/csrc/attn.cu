@@ -310,13 +310,18 @@ attn_decode_kernel(const attn_params p)
         }
         *reinterpret_cast<float4 *>(w + kRecAcc + 4 * lane) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
     }
-    // the last CTA of this kv head merges the splits
-    __threadfence();
+    // the last CTA of this kv head merges the splits: the barrier orders the
+    // CTA's record writes before thread 0's count, whose release (gpu scope,
+    // cumulative) publishes them; its acquire, and the barrier after it,
+    // order every other CTA's records before the merge's reads
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(&p.cnt[kv], 1u) == (unsigned)p.splits - 1;
+    if (threadIdx.x == 0) {
+        unsigned prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.cnt + kv) : "memory");
+        last = prev == (unsigned)p.splits - 1;
+    }
     __syncthreads();
     if (!last) return;
-    __threadfence();
     // splits that hold positions (the rest are empty for this token)
     const int used = (s + span - 1) / span;
     for (int hg = warp; hg < G; hg += kWarps) {
