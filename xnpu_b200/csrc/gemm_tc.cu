@@ -147,6 +147,26 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int j)
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
 }
 
+// One dequant warp's view of one packed chunk: lane l's 16 code bytes and its
+// row pair's two group scales (rows g, g + 8: bytes g * 8 of the scale run).
+// Explicit ld.shared / st.shared: generic accesses here measured 4-5 % slower
+// over the whole GEMM (m = 32 .. 2048).
+struct PkChunk {
+    uint4 cw;
+    uint2 sw;
+};
+__device__ __forceinline__ PkChunk load_pk_chunk(const uint8_t *up, int lane)
+{
+    const uint32_t u = xq4d::smem_u32(up);
+    return {xq4d::lds_v4(u + lane * 16), xq4d::lds_v2(u + XQ4G_CODE_BYTES + (lane >> 2) * 8)};
+}
+__device__ __forceinline__ void store_a16(uint8_t *a, uint32_t off, uint4 v)
+{
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(xq4d::smem_u32(a) + off), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 // ------------------------------------------------------------ cluster helpers
 __device__ __forceinline__ uint32_t cluster_map(uint32_t local_saddr, uint32_t rank)
 {
@@ -199,7 +219,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             int kc_n, int m, int bn, int P, int D, int S, int tile0, int tiles_n, void *__restrict__ y, int out_f32)
 {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // the 1024-byte aligned base as an offset into the shared array: the
+    // compiler keeps every access through it in the shared state space (an
+    // integer round trip of the pointer made them generic: 1.5-2 % slower)
+    uint8_t *smem = smem_raw + ((1024u - (xq4d::smem_u32(smem_raw) & 1023u)) & 1023u);
     const int X = D, A = D;                                 // x and A stages advance together
     uint8_t *at = smem;                                     // [D][128][64] bf16, swizzled
     uint8_t *xt = at + (size_t)A * kATileBytes;             // [D][bn][64] bf16, swizzled
@@ -351,8 +374,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             }
             // the box lands as [row block][chunk][576 B]
             const uint8_t *up = pk + (size_t)sp * kPackedBytes + (warp * kPkChunks + c) * XQ4G_UNIT_BYTES;
-            const uint4 cw = *reinterpret_cast<const uint4 *>(up + lane * 16);
-            const uint2 sw = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+            const PkChunk pc = load_pk_chunk(up, lane);
+            const uint4 cw = pc.cw;
+            const uint2 sw = pc.sw;
             __syncwarp();
             const bool stage_done = c == kPkChunks - 1 || i == nk - 1;
             if (lane == 0 && stage_done) xq4d::mbar_arrive(&pempty[sp]);  // packed stage read: refill it
@@ -381,10 +405,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CU
             }
             uint8_t *a = at + (size_t)sa * kATileBytes;
             const int r0 = warp * XQ4G_ROWS + g;  // swizzle chunk of (row, group G) = 4G + t
-            *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * gsel + t)) = gsel ? lo[1] : lo[0];
-            *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * (1 - gsel) + t)) = gsel ? lo[0] : lo[1];
-            *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * gsel + t)) = gsel ? hi[1] : hi[0];
-            *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * (1 - gsel) + t)) = gsel ? hi[0] : hi[1];
+            store_a16(a, sw128_offset(r0, 4 * gsel + t), gsel ? lo[1] : lo[0]);
+            store_a16(a, sw128_offset(r0, 4 * (1 - gsel) + t), gsel ? lo[0] : lo[1]);
+            store_a16(a, sw128_offset(r0 + 8, 4 * gsel + t), gsel ? hi[1] : hi[0]);
+            store_a16(a, sw128_offset(r0 + 8, 4 * (1 - gsel) + t), gsel ? hi[0] : hi[1]);
             // each writer makes its stores visible to the tensor core; one
             // arrival per warp (256 arrivals on one mbarrier serialise: they
             // cost ~1 us per stage, measured)
@@ -504,7 +528,7 @@ gemm_pt_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__
                int m, int bn, int P, int D, int tile0, int count, int tiles_n, void *__restrict__ y, int out_f32)
 {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t *smem = smem_raw + ((1024u - (xq4d::smem_u32(smem_raw) & 1023u)) & 1023u);  // as gemm_kernel
     const uint32_t xbytes = (uint32_t)x_tile_bytes(bn);
     uint8_t *at = smem;                            // [D][128][64] bf16, swizzled
     uint8_t *xt = at + (size_t)D * kATileBytes;     // [D][bn][64] bf16, swizzled
@@ -659,8 +683,9 @@ gemm_pt_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__
                     break;
                 }
                 const uint8_t *up = pk + (size_t)sp * kPackedBytes + (warp * kPkChunks + c) * XQ4G_UNIT_BYTES;
-                const uint4 cw = *reinterpret_cast<const uint4 *>(up + lane * 16);
-                const uint2 sw = *reinterpret_cast<const uint2 *>(up + XQ4G_CODE_BYTES + g * 8);
+                const PkChunk pc = load_pk_chunk(up, lane);
+                const uint4 cw = pc.cw;
+                const uint2 sw = pc.sw;
                 __syncwarp();
                 // a tile's packed stages hold 4 chunks each, the last one
                 // whatever remains of K
@@ -692,10 +717,10 @@ gemm_pt_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__
                 }
                 uint8_t *a = at + (size_t)sa * kATileBytes;
                 const int r0 = warp * XQ4G_ROWS + g;
-                *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * gsel + t)) = gsel ? lo[1] : lo[0];
-                *reinterpret_cast<uint4 *>(a + sw128_offset(r0, 4 * (1 - gsel) + t)) = gsel ? lo[0] : lo[1];
-                *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * gsel + t)) = gsel ? hi[1] : hi[0];
-                *reinterpret_cast<uint4 *>(a + sw128_offset(r0 + 8, 4 * (1 - gsel) + t)) = gsel ? hi[0] : hi[1];
+                store_a16(a, sw128_offset(r0, 4 * gsel + t), gsel ? lo[1] : lo[0]);
+                store_a16(a, sw128_offset(r0, 4 * (1 - gsel) + t), gsel ? lo[0] : lo[1]);
+                store_a16(a, sw128_offset(r0 + 8, 4 * gsel + t), gsel ? hi[1] : hi[0]);
+                store_a16(a, sw128_offset(r0 + 8, 4 * (1 - gsel) + t), gsel ? hi[0] : hi[1]);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) xq4d::mbar_arrive(&afull[sa]);
