@@ -240,9 +240,8 @@ w4a8_kernel(const uint8_t *__restrict__ pack, int n, int k, int nb, int kc_n, co
     const uint32_t xrow = xq4d::smem_u32(xq + (size_t)(g < m ? g : 0) * kp);  // B column g = token g
     const uint32_t tab_s = xq4d::smem_u32(tab), ring_s = xq4d::smem_u32(ring);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    int slot = 0, rbl = 0, kc0 = 0;
+    int slot = 0, kc0 = 0;
     uint32_t phase = 0;
-    (void)rbl;
     for (int i = 0; i < total; i++) {
         const uint32_t stage = ring_s + (uint32_t)slot * kStageBytes;
         if (!xq4d::mbar_wait(&full[slot], phase)) {
