@@ -130,3 +130,20 @@ def test_attention_position_outside_the_cache(dev):
     assert np.array_equal(from_dev_bf16(kd), kc) and np.array_equal(from_dev_bf16(vd), vc)
     assert bool((out == 7.0).all())
     attn.destroy()
+
+
+def test_attention_handles_of_different_sizes(dev):
+    """A handle created after a larger one (a smaller shared-memory plan) must
+    leave the larger one's launches valid: the kernel's shared-memory limit is
+    one per-device attribute, raised by creates and never lowered."""
+    heads, nkv, base = 32, 8, 500000.0
+    big = hal.Attention(dev, heads, nkv, 4096, base)
+    small = hal.Attention(dev, heads, nkv, 64, base)
+    for attn, cache_seq, pos in ((big, 4096, 1000), (small, 64, 40), (big, 4096, 4095)):
+        qkv, kc, vc, w = _case(heads, nkv, cache_seq, pos, 200 + pos, True)
+        got, gk, gv = _run(dev, attn, qkv, kc, vc, w, pos)
+        want, wk, wv = _oracle(qkv, kc, vc, w, heads, nkv, cache_seq, pos, base)
+        _check(got, want, gk, wk, gv, wv, f"cache {cache_seq} pos={pos}")
+    assert dev.fault() == 0
+    small.destroy()
+    big.destroy()

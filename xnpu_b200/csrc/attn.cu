@@ -35,6 +35,7 @@
 #include <stdint.h>
 #include <string.h>
 #include <algorithm>
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -392,6 +393,20 @@ struct xq4_attn {
     size_t smem;
 };
 
+// The kernel's dynamic shared-memory limit is one attribute per device for
+// every attention handle: it only ever grows, so that creating a handle with
+// a smaller plan leaves the launches of an earlier, larger one valid.
+static cudaError_t raise_smem_limit(int ordinal, size_t smem)
+{
+    static std::mutex mu;
+    static size_t limit[64];
+    std::lock_guard<std::mutex> lock(mu);
+    if (ordinal >= 0 && ordinal < 64 && limit[ordinal] >= smem) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && ordinal >= 0 && ordinal < 64) limit[ordinal] = smem;
+    return e;
+}
+
 extern "C" int xq4_attn_create(xq4_device *dev, int heads, int nkv, int cache_seq, float rope_base, xq4_attn **out)
 {
     xq4_clear_error();
@@ -445,8 +460,7 @@ extern "C" int xq4_attn_create(xq4_device *dev, int heads, int nkv, int cache_se
     if (e == cudaSuccess) e = cudaMalloc(&a->ws, ws_bytes);
     if (e == cudaSuccess) e = cudaMalloc(&a->cnt, sizeof(unsigned) * nkv);
     if (e == cudaSuccess) e = cudaMemset(a->cnt, 0, sizeof(unsigned) * nkv);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   (int)a->smem);
+    if (e == cudaSuccess) e = raise_smem_limit(ordinal, a->smem);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaGetLastError();
